@@ -1,0 +1,216 @@
+/*
+ * ipuc.h — C ABI of the B200 operator-catalog backend (libipuc.so).
+ *
+ * One extern "C" entry per reference TileKernelSpec family
+ * (crates/ipu-codegen/src/operator.rs:57-96).  Each entry replaces the
+ * supervisor-ABI tile kernel the reference's ipu-codegen calls per tile
+ * (crates/ipu-codegen/src/kernel.rs:1215-1382: m2 output, m3.. inputs, then
+ * scalars), with device pointers in place of tile SRAM addresses and one GPU
+ * shard in place of one tile's work list.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer owned by the caller.  The library never
+ *    allocates device memory on these paths (reference: kernels never
+ *    allocate; crates/ipu-codegen/src/operator.rs:533-537 for aliasing).
+ *  - Calls are stream-ordered on `stream` (a cudaStream_t; NULL = legacy
+ *    default stream) and return before the kernel finishes.
+ *  - Arguments are validated on the host before any launch, mirroring
+ *    validate_kernel_run (kernel.rs:1384-1435).  On failure nothing is
+ *    launched, an ipuc_status error is returned and
+ *    ipuc_last_error_string() describes it (thread-local).
+ *  - f16 = IEEE binary16, f32 = IEEE binary32.  "row-major" matrices are dense
+ *    with the stated leading dimension in elements.
+ */
+#ifndef IPUC_H
+#define IPUC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ipuc_stream; /* == cudaStream_t */
+
+/* Host-side Result<_, KernelAbiError | KernelMaterializationError>
+ * (kernel.rs:140-176) becomes a status code. */
+typedef enum {
+  IPUC_OK = 0,
+  IPUC_ERR_INVALID_ARGUMENT = 1, /* shape/arity/count checks (KernelAbiError::*) */
+  IPUC_ERR_UNSUPPORTED = 2,      /* KernelAvailability::Required / unsupported geometry */
+  IPUC_ERR_ALIGNMENT = 3,        /* pointer or leading-dimension alignment */
+  IPUC_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
+  IPUC_ERR_NCCL = 5,             /* a collective failed */
+  IPUC_ERR_DEVICE_TIMEOUT = 6    /* a bounded device wait gave up (error word set) */
+} ipuc_status;
+
+/* Precision (operator.rs Precision, F16/F32 only). */
+typedef enum { IPUC_F16 = 0, IPUC_F32 = 1 } ipuc_precision;
+
+/* ElementOrder (crates/ipu-codegen/src/layout.rs:7-45). */
+typedef enum {
+  IPUC_ORDER_ROW_MAJOR = 0,
+  IPUC_ORDER_AMP_LEFT = 1,
+  IPUC_ORDER_AMP_TRANSPOSED_LEFT = 2,
+  IPUC_ORDER_AMP_TRANSPOSED_RIGHT = 3,
+  IPUC_ORDER_AMP_OUTPUT = 4,
+  IPUC_ORDER_AMP_TRANSPOSED_OUTPUT = 5,
+  IPUC_ORDER_BLOCK_MAJOR = 6,           /* BlockMajorOrder::Matrix{row_block, column_block} */
+  IPUC_ORDER_BLOCK_MAJOR_TRANSPOSED = 7 /* BlockMajorOrder::TransposedMatrix{..} */
+} ipuc_order;
+
+/* Library / device information ------------------------------------------ */
+const char *ipuc_version(void);
+const char *ipuc_status_string(ipuc_status status);
+/* Thread-local description of the last error returned on this thread. */
+const char *ipuc_last_error_string(void);
+/* Reads and clears the device error word set by bounded waits inside kernels
+ * on the current device (synchronises `stream`).  Reference: the device
+ * "fails" only by host-side timeout (device/static_runtime.S:487-488). */
+ipuc_status ipuc_device_status(ipuc_stream stream);
+
+/* FillZero: device/static_runtime.S:269-316, ABI kernel.rs:1224-1229.
+ * bytes % 8 == 0 (validate_kernel_run, kernel.rs:1425-1434). */
+ipuc_status ipuc_fill_zero(void *out, uint64_t bytes, ipuc_stream stream);
+
+/* Gemm ------------------------------------------------------------------- */
+/* Replaces ipu_stack_gemm_f16_{init,accumulate}_* (device/gemm_f16_amp.S:
+ * 186-440; spec TileKernelSpec::Gemm, operator.rs:59-66; expansion
+ * lower_blocked_gemm, low.rs:3465-3560).
+ *   C[m x n] = epilogue(A[m x k] . B[k x n] (+ C if IPUC_GEMM_ACCUMULATE))
+ * A row-major (lda >= k).  B row-major [k x n] (ldb >= n), or with
+ * IPUC_GEMM_B_TRANSPOSED stored as [n x k] (ldb >= k).  C row-major (ldc >= n),
+ * f16, or f32 with IPUC_GEMM_OUT_F32 (split-K partials).  fp32 accumulation
+ * over the whole k in tensor memory.  Requirements: k % 64 == 0,
+ * m, n >= 1, 16-byte aligned pointers, lda/ldb/ldc multiples of 8 elements.
+ * Epilogue order: acc (+C) -> round to C's precision -> GELU -> store.
+ * mode Accumulate == IPUC_GEMM_ACCUMULATE (GemmKernelMode, operator.rs:98-102). */
+enum {
+  IPUC_GEMM_ACCUMULATE = 1u << 0,
+  IPUC_GEMM_B_TRANSPOSED = 1u << 1,
+  IPUC_GEMM_OUT_F32 = 1u << 2,
+  IPUC_GEMM_EPILOGUE_GELU = 1u << 3
+};
+ipuc_status ipuc_gemm_f16(void *c, const void *a, const void *b, int64_t m, int64_t n, int64_t k,
+                          int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags,
+                          ipuc_stream stream);
+
+/* Batched form: `batch` independent GEMMs at the given element strides
+ * (batched-gemm-smoke, crates/ipu-tests/src/main.rs:201-220). */
+ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t batch,
+                                  int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+                                  int64_t ldc, int64_t stride_a, int64_t stride_b,
+                                  int64_t stride_c, uint32_t flags, ipuc_stream stream);
+
+/* Replaces ipu_stack_gemm_f32_{init,accumulate}_* (device/gemm_f32_64_amp.S:
+ * 129-385).  f32 in, f32 out, C (+)= A.B with three-pass TF32 splitting on the
+ * tensor cores (hi.hi + hi.lo + lo.hi), accurate to an f32 tolerance.
+ * workspace: caller-provided device scratch of ipuc_gemm_f32_workspace_bytes()
+ * bytes (the hi/lo split operands), 256-byte aligned.  Requirements as
+ * ipuc_gemm_f16 except k % 32 == 0 and lda/ldb/ldc multiples of 4. */
+uint64_t ipuc_gemm_f32_workspace_bytes(int64_t m, int64_t n, int64_t k);
+ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, int64_t m, int64_t n, int64_t k,
+                          int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, void *workspace,
+                          uint64_t workspace_bytes, ipuc_stream stream);
+
+/* Gelu: ipu_stack_gelu_tanh_approx_f16 (device/gelu_f16.S:7-148; ABI
+ * kernel.rs:1251-1263; element_count even, kernel.rs:1400-1413).
+ * out may equal in. */
+ipuc_status ipuc_gelu_f16(void *out, const void *in, uint64_t element_count, ipuc_stream stream);
+
+/* ReductionSum: ipu_stack_reduce_sum_f16 (device/reduce_add_f16.S:7-72; ABI
+ * kernel.rs:1264-1274, scalars num_partials = partials - 1 and element_count;
+ * partials >= 2 and element_count % 8 == 0, kernel.rs:1414-1423).
+ *   out = initial + sum_{p < num_partials} remote[p * element_count + i]
+ * in_precision F16 (the reference's kernel) or F32 (split-K fp32 partials);
+ * out is f16.  fp32 accumulation, one rounding. */
+ipuc_status ipuc_reduce_sum(void *out, const void *initial, const void *remote, uint32_t num_partials,
+                            uint64_t element_count, ipuc_precision in_precision, ipuc_stream stream);
+
+/* Add (kernel.rs:1275-1287, KernelAvailability::Required in the reference):
+ * out[i] = left[i % lp] + right[i % rp] with lp/rp = 0 meaning no broadcast
+ * (scalars element_count, left_broadcast_stride, right_broadcast_stride). */
+ipuc_status ipuc_add_f16(void *out, const void *left, const void *right, uint64_t element_count,
+                         uint64_t left_broadcast_stride, uint64_t right_broadcast_stride,
+                         ipuc_stream stream);
+
+/* Cast (kernel.rs:1313-1318, Required in the reference): f16 <-> f32. */
+ipuc_status ipuc_cast(void *out, ipuc_precision to, const void *in, ipuc_precision from,
+                      uint64_t element_count, ipuc_stream stream);
+
+/* FlashAttention: flash_attention_online_f16 (device/flash_attention_online_f16.
+ * cpp:61-143; ABI kernel.rs:1288-1300; shape key kernel.rs:125-132).
+ * Exact non-causal softmax(Q K^T * scale) V per stream:
+ *   Q [matrices][query_rows][head_dim], K [matrices][key_rows][head_dim],
+ *   V [matrices][key_rows][head_dim] f16 row-major; out [matrices][query_rows]
+ *   [head_dim] in out_precision (F32 = the reference vertex; F16 = BASELINE).
+ * scale <= 0 selects 1/sqrt(head_dim) (AttentionScale::InverseSqrtQueryWidth).
+ * fp32 running max/denominator.  head_dim == 128 (tensor-core path) or
+ * head_dim % 8 == 0 && head_dim <= 256 (general path). */
+ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_precision, const void *q,
+                                     const void *k, const void *v, int64_t matrices,
+                                     int64_t query_rows, int64_t key_rows, int64_t head_dim,
+                                     float scale, ipuc_stream stream);
+
+/* AttentionSoftmax (device/attention_softmax_f16.cpp:63-139, asm variant
+ * device/attention_stages_f16.S:54-695): one key block per call.
+ *   scores  f16 panels [key_block_columns/16][query_rows][16]
+ *   weights f16 in the same order = exp(s*scale - max*scale), padding keys
+ *           (>= key_rows) 0, followed in memory by query_rows f32 scaled maxima
+ *           and query_rows f32 denominators (attention_softmax_f16.cpp:89-91).
+ * scale = 1/sqrt(head_dimension).  key_block_columns % 16 == 0. */
+ipuc_status ipuc_attention_softmax_f16(void *weights, const void *scores, int64_t query_rows,
+                                       int64_t key_rows, int64_t key_block_columns,
+                                       int64_t head_dimension, ipuc_stream stream);
+
+/* AttentionMerge (device/attention_stages_f16.S:698-855).
+ *   acc   f32 rows of padded_value_dimension; row r's {max, denominator} are
+ *         stored at acc[r][value_dimension], acc[r][value_dimension+1]
+ *         (so padded_value_dimension >= value_dimension + 2).
+ *   block f16 PV panels [ceil(value_dimension/16)][query_rows][16].
+ *   state the softmax stage's f32 maxima[query_rows] then denominators[query_rows].
+ * initial: acc = block; final: acc *= 1/denominator. */
+ipuc_status ipuc_attention_merge_f16(float *acc, const void *block, const float *state,
+                                     int64_t query_rows, int64_t value_dimension,
+                                     int64_t padded_value_dimension, int initial, int final_block,
+                                     ipuc_stream stream);
+
+/* Rearrange row-major -> {AMP-Left (0), AMP-TransposedRight (1), BlockMajor
+ * (2)} f16, bit-exact with zero padding (device/rearrange_f16.cpp:36-155,
+ * device/rearrange_amp_left_f16.S:42-140, device/rearrange_transposed_right_f16.S
+ * :15-60, device/rearrange_block_major_f16.S:21-116; scalars kernel.rs:1149-1193
+ * logical/physical rows/columns and target_order; selection kernel.rs:363-498).
+ * src: `matrices` row-major [logical_rows x logical_columns]; dst: `matrices`
+ * physical [physical_rows x physical_columns].  row_block/column_block apply to
+ * BlockMajor; AMP-TransposedRight uses column_block rows per panel (16 in the
+ * reference).  logical_columns even; physical_columns % 16 == 0. */
+ipuc_status ipuc_rearrange_f16(void *dst, const void *src, int64_t matrices, int64_t logical_rows,
+                               int64_t physical_rows, int32_t target_order,
+                               int64_t logical_columns, int64_t physical_columns,
+                               int64_t row_block, int64_t column_block, ipuc_stream stream);
+
+/* Unpack AMP-Output (source_order 0) / AMP-TransposedLeft (1) -> row-major f16
+ * (device/unpack_amp_f16.cpp:40-81; build kernel.rs:321-362).  dst is
+ * `matrices` row-major [physical_rows x physical_columns], zero outside the
+ * logical region. */
+ipuc_status ipuc_unpack_f16(void *dst, const void *src, int32_t source_order, int64_t matrices,
+                            int64_t logical_rows, int64_t physical_rows, int64_t logical_columns,
+                            int64_t physical_columns, ipuc_stream stream);
+
+/* General element-order conversion (kernel.rs:1365-1370, "ipu_stack_rearrange",
+ * Required in the reference): any ipuc_order -> any ipuc_order for `matrices`
+ * [rows x columns] f16 matrices (both physical extents equal), bit-exact. */
+ipuc_status ipuc_convert_order_f16(void *dst, ipuc_order to, const void *src, ipuc_order from,
+                                   int64_t matrices, int64_t rows, int64_t columns,
+                                   int64_t row_block, int64_t column_block, ipuc_stream stream);
+
+/* SplitHeads (graph.rs:336-343; evaluator diagnostic.rs:685-709):
+ * [batch, rows, heads*channels] -> [batch*heads, rows, channels], f16. */
+ipuc_status ipuc_split_heads_f16(void *out, const void *in, int64_t batch, int64_t rows,
+                                 int64_t heads, int64_t channels, ipuc_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* IPUC_H */

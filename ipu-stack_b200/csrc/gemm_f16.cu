@@ -1,0 +1,328 @@
+// FP16 GEMM on the 5th-generation tensor cores: the B200 counterpart of the
+// reference's gemm_f16_amp tile kernels (device/gemm_f16_amp.S:186-440; spec
+// TileKernelSpec::Gemm, crates/ipu-codegen/src/operator.rs:59-66).
+//
+// Design (one persistent CTA per SM, warp-specialised):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [64 x 256] per
+//               k-block into a 4-stage shared-memory ring (128-byte swizzle).
+//   warp 1      MMA issuer: allocates 512 TMEM columns (two 128x256 f32
+//               accumulators), issues tcgen05.mma M=128 N=256 K=16 from one
+//               thread, commits stage releases and accumulator-ready signals.
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (each warp owns its
+//               32-lane TMEM quarter), optional accumulate with C, rounding,
+//               fused tanh-GELU, f16 or f32 stores.  Double-buffered TMEM lets
+//               the epilogue of tile i overlap the MMAs of tile i+1.
+// The whole K loop accumulates in TMEM (fp32), so the reference's f16 partial
+// round trip between 64-wide K blocks (gemm_f16_amp.S:363-437) disappears.
+// Every mbarrier wait is bounded; on timeout the kernel records an error word
+// and all roles drain to the teardown (no trap).
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+namespace ipuc {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;          // 16 KB
+constexpr int B_BYTES = BN * BK * 2;          // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;             // 512
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int GROUP_M = 16;
+
+struct GemmParams {
+  void *c;
+  int64_t m, n, k, batch;
+  int64_t ldc, stride_c;
+  int32_t tiles_m, tiles_n, k_blocks;
+  int64_t num_tiles;
+  uint32_t flags;
+  uint32_t *err;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmParams &p, int64_t t, int &b, int &mt, int &nt) {
+  const int64_t per = (int64_t)p.tiles_m * p.tiles_n;
+  b = (int)(t / per);
+  const int64_t r = t % per;
+  const int64_t in_group = (int64_t)GROUP_M * p.tiles_n;
+  const int64_t g = r / in_group;
+  const int first = (int)(g * GROUP_M);
+  const int gs = min(p.tiles_m - first, GROUP_M);
+  const int64_t w = r % in_group;
+  mt = first + (int)(w % gs);
+  nt = (int)(w / gs);
+}
+
+template <bool kBKMajor>
+__global__ void __launch_bounds__(192, 1)
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tmem_full = empty + STAGES;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tmem_empty + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int b, mt, nt;
+        tile_coords(p, t, b, mt, nt);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *a_s = smem + s * STAGE_BYTES;
+          uint8_t *b_s = a_s + A_BYTES;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          tma_load_3d(a_s, &tmA, &full[s], kb * BK, mt * BM, b);
+          if (kBKMajor) {
+            tma_load_3d(b_s, &tmB, &full[s], kb * BK, nt * BN, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_s + j * 8192, &tmB, &full[s], nt * BN + j * 64, kb * BK, b);
+          }
+        }
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_PRODUCER);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(BM, BN, /*f16*/ 0, false, !kBKMajor);
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const uint32_t buf = local & 1u, use = local >> 1;
+        if (!mbar_wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = make_smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bdesc = kBKMajor ? make_smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B)
+                                            : make_smem_desc(b_addr + k * 2048, 8192, 1024, kSwizzle128B);
+            mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&tmem_full[buf]);
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_MMA);
+        *abort_flag = 1;
+      }
+    }
+  } else {
+    // Epilogue: 128 threads; warp w owns TMEM lanes [32*(w%4), 32*(w%4)+32).
+    const int quarter = warp & 3;
+    const bool out_f32 = (p.flags & IPUC_GEMM_OUT_F32) != 0;
+    const bool accumulate = (p.flags & IPUC_GEMM_ACCUMULATE) != 0;
+    const bool gelu = (p.flags & IPUC_GEMM_EPILOGUE_GELU) != 0;
+    const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0);
+    uint32_t local = 0;
+    for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      const uint32_t buf = local & 1u, use = local >> 1;
+      if (!mbar_wait_bounded(&tmem_full[buf], use & 1u, abort_flag)) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_EPILOGUE);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int b, mt, nt;
+      tile_coords(p, t, b, mt, nt);
+      const int64_t row = (int64_t)mt * BM + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + buf * BN + chunk * 32 + ((uint32_t)(quarter * 32) << 16), r);
+        tmem_wait_ld();
+        const int64_t col0 = (int64_t)nt * BN + chunk * 32;
+        if (!row_ok || col0 >= p.n) continue;
+        const bool full_chunk = vec_ok && (col0 + 32 <= p.n);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (out_f32) {
+          float *cp = static_cast<float *>(p.c) + b * p.stride_c + row * p.ldc + col0;
+          if (full_chunk) {
+            float4 *c4 = reinterpret_cast<float4 *>(cp);
+            if (accumulate) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 o = c4[j];
+                v[4 * j] += o.x; v[4 * j + 1] += o.y; v[4 * j + 2] += o.z; v[4 * j + 3] += o.w;
+              }
+            }
+            if (gelu) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu_f32(v[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) c4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+              float x = v[j];
+              if (accumulate) x += cp[j];
+              if (gelu) x = gelu_f32(x);
+              cp[j] = x;
+            }
+          }
+        } else {
+          uint16_t *cp = static_cast<uint16_t *>(p.c) + b * p.stride_c + row * p.ldc + col0;
+          if (full_chunk) {
+            uint4 *c4 = reinterpret_cast<uint4 *>(cp);
+            if (accumulate) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 o = c4[j];
+                const uint16_t *h = reinterpret_cast<const uint16_t *>(&o);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[8 * j + e] += h2f(h[e]);
+              }
+            }
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float x0 = v[2 * j], x1 = v[2 * j + 1];
+              if (gelu) {
+                x0 = gelu_f32(__half2float(__float2half_rn(x0)));
+                x1 = gelu_f32(__half2float(__float2half_rn(x1)));
+              }
+              packed[j] = pack_h2(x0, x1);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              c4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+              float x = v[j];
+              if (accumulate) x += h2f(cp[j]);
+              if (gelu) x = gelu_f32(__half2float(__float2half_rn(x)));
+              cp[j] = f2h(x);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch, int64_t m, int64_t n, int64_t k,
+                            int64_t lda, int64_t ldb, int64_t ldc, int64_t sa, int64_t sb, int64_t sc,
+                            uint32_t flags, cudaStream_t stream) {
+  IPUC_CHECK_ARG(m >= 0 && n >= 0 && k >= 0 && batch >= 0, "gemm_f16: negative extent");
+  IPUC_CHECK_ARG((flags & ~0xfu) == 0, "gemm_f16: unknown flag");
+  if (m == 0 || n == 0 || batch == 0) return IPUC_OK;
+  IPUC_CHECK_ARG(k > 0, "gemm_f16: k must be positive");
+  IPUC_CHECK_ARG(a && b && c, "gemm_f16: null pointer");
+  const bool bt = (flags & IPUC_GEMM_B_TRANSPOSED) != 0;
+  IPUC_CHECK_ARG(lda >= k && ldc >= n && ldb >= (bt ? k : n), "gemm_f16: leading dimension too small");
+  IPUC_CHECK_ALIGN(aligned(a, 16) && aligned(b, 16) && aligned(c, 16), "gemm_f16: pointers must be 16-byte aligned");
+  IPUC_CHECK_ALIGN(lda % 8 == 0 && ldb % 8 == 0 && k % 8 == 0,
+                   "gemm_f16: lda, ldb and k must be multiples of 8 elements (16-byte TMA rows)");
+  IPUC_CHECK_ALIGN(batch == 1 || (sa % 8 == 0 && sb % 8 == 0), "gemm_f16: batch strides must be multiples of 8");
+  IPUC_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31) && batch < (1ll << 31), "gemm_f16: extent too large");
+  CUtensorMap ta, tb;
+  ipuc_status st = make_map_3d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, batch, lda, batch > 1 ? sa : 0, BK, BM);
+  if (st != IPUC_OK) return st;
+  if (bt) st = make_map_3d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, k, n, batch, ldb, batch > 1 ? sb : 0, BK, BN);
+  else st = make_map_3d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, n, k, batch, ldb, batch > 1 ? sb : 0, 64, BK);
+  if (st != IPUC_OK) return st;
+  GemmParams p;
+  p.c = c;
+  p.m = m; p.n = n; p.k = k; p.batch = batch;
+  p.ldc = ldc;
+  p.stride_c = batch > 1 ? sc : 0;
+  p.tiles_m = (int32_t)((m + BM - 1) / BM);
+  p.tiles_n = (int32_t)((n + BN - 1) / BN);
+  p.k_blocks = (int32_t)((k + BK - 1) / BK);
+  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
+  p.flags = flags;
+  p.err = device_error_word();
+  const int grid = (int)(p.num_tiles < sm_count() ? p.num_tiles : sm_count());
+  if (bt) {
+    IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    gemm_f16_kernel<true><<<grid, 192, SMEM_BYTES, stream>>>(ta, tb, p);
+  } else {
+    IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    gemm_f16_kernel<false><<<grid, 192, SMEM_BYTES, stream>>>(ta, tb, p);
+  }
+  return check_launch("gemm_f16_kernel");
+}
+
+}  // namespace
+}  // namespace ipuc
+
+using namespace ipuc;
+
+extern "C" ipuc_status ipuc_gemm_f16(void *c, const void *a, const void *b, int64_t m, int64_t n, int64_t k,
+                                     int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, ipuc_stream stream) {
+  return launch_gemm_f16(c, a, b, 1, m, n, k, lda, ldb, ldc, 0, 0, 0, flags, stream);
+}
+
+extern "C" ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t batch, int64_t m,
+                                             int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                             int64_t stride_a, int64_t stride_b, int64_t stride_c, uint32_t flags,
+                                             ipuc_stream stream) {
+  return launch_gemm_f16(c, a, b, batch, m, n, k, lda, ldb, ldc, stride_a, stride_b, stride_c, flags, stream);
+}

@@ -1,0 +1,352 @@
+// Bit-exact f16 element-order conversions: the rearrange_* and unpack_amp_*
+// tile kernels of the reference (device/rearrange_f16.cpp:36-155,
+// device/rearrange_amp_left_f16.S, device/rearrange_block_major_f16.S,
+// device/rearrange_transposed_right_f16.S, device/unpack_amp_f16.cpp:40-81),
+// the general order conversion the reference leaves unimplemented
+// (crates/ipu-codegen/src/kernel.rs:1365-1370) and SplitHeads
+// (crates/ipu-tests/src/diagnostic.rs:685-709).
+//
+// Every packed order of crates/ipu-codegen/src/storage.rs stores each 16x16
+// micro-block of a matrix as 256 contiguous elements, with an order-specific
+// permutation inside the block (derivation per order in block_base /
+// block_offset below).  The kernel therefore moves one micro-block per warp:
+// each lane reads one 16-byte chunk of the source block, the warp transposes
+// through a 16x16 shared-memory tile, and each lane writes one 16-byte chunk
+// of the destination block.  Global traffic is one read and one write of
+// each byte in full 32-byte sectors (HBM-bound, no tensor cores).
+#include "common.cuh"
+
+namespace ipuc {
+namespace {
+
+struct Side {
+  void *ptr;
+  int32_t order;
+  int64_t rows, cols;  // physical extents of one matrix
+  int64_t ld;          // row-major leading dimension (elements)
+  int64_t mstride;     // elements between matrices
+  int64_t rb, cb;      // block-major row/column block
+  int32_t vec;         // 16-byte vector accesses allowed on the row-major side
+};
+
+// storage.rs:333-340 AMP-Output pair swizzle and its inverse (storage.rs:689-694).
+__device__ __forceinline__ int swz(int c) {
+  int lp = c >> 1, pp = (lp & 3) * 2 + (lp >> 2);
+  return pp * 2 + (c & 1);
+}
+__device__ __forceinline__ int unswz(int pc) {
+  int pp = pc >> 1, lp = (pp & 1) * 4 + (pp >> 1);
+  return lp * 2 + (pc & 1);
+}
+
+// Element index of the first element of micro-block (br, bc) within a matrix.
+//   AMP-Left            idx = (c/16)*R*16 + r*16 + c%16                 (storage.rs:316-325)
+//   AMP-TransposedLeft  idx = (r/16)*C*16 + c*16 + r%16                 (storage.rs:327-329)
+//   AMP-TransposedRight idx = ((r/16)*(C/16) + c/16)*256 + (r%16)*16 + c%16  (storage.rs:326,353-371)
+//   AMP-Output          idx = (c/16)*R*16 + r*16 + swz(c%16)           (storage.rs:330-340)
+//   AMP-TransposedOut.  idx = (r/16)*C*16 + c*16 + swz(r%16)           (storage.rs:341-343)
+//   BlockMajor{rb,cb}   idx = panel*16*cb + (c%cb)*16 + r%16, panel =
+//                       (r/rb)*(C/cb)*(rb/16) + (c/cb)*(rb/16) + (r%rb)/16   (storage.rs:372-426)
+//   BlockMajor^T        the same with (r, c, R, C) -> (c, r, C, R)
+__device__ __forceinline__ int64_t block_base(const Side &s, int64_t br, int64_t bc) {
+  const int64_t R = s.rows, C = s.cols;
+  switch (s.order) {
+    case IPUC_ORDER_AMP_LEFT:
+    case IPUC_ORDER_AMP_OUTPUT:
+      return bc * R * 16 + br * 256;
+    case IPUC_ORDER_AMP_TRANSPOSED_LEFT:
+    case IPUC_ORDER_AMP_TRANSPOSED_OUTPUT:
+      return br * C * 16 + bc * 256;
+    case IPUC_ORDER_AMP_TRANSPOSED_RIGHT:
+      return (br * (C / 16) + bc) * 256;
+    case IPUC_ORDER_BLOCK_MAJOR: {
+      const int64_t r0 = br * 16, c0 = bc * 16, rg = s.rb / 16;
+      const int64_t panel = (r0 / s.rb) * (C / s.cb) * rg + (c0 / s.cb) * rg + (r0 % s.rb) / 16;
+      return panel * 16 * s.cb + (c0 % s.cb) * 16;
+    }
+    case IPUC_ORDER_BLOCK_MAJOR_TRANSPOSED: {
+      const int64_t r0 = bc * 16, c0 = br * 16, rg = s.rb / 16;  // transposed view
+      const int64_t panel = (r0 / s.rb) * (R / s.cb) * rg + (c0 / s.cb) * rg + (r0 % s.rb) / 16;
+      return panel * 16 * s.cb + (c0 % s.cb) * 16;
+    }
+  }
+  return 0;
+}
+
+// Whether the block stores its elements rows-outer (offset = rr*16 + f(cc)).
+__device__ __forceinline__ bool rows_outer(int32_t order) {
+  return order == IPUC_ORDER_AMP_LEFT || order == IPUC_ORDER_AMP_TRANSPOSED_RIGHT ||
+         order == IPUC_ORDER_AMP_OUTPUT || order == IPUC_ORDER_BLOCK_MAJOR_TRANSPOSED;
+}
+__device__ __forceinline__ bool swizzled(int32_t order) {
+  return order == IPUC_ORDER_AMP_OUTPUT || order == IPUC_ORDER_AMP_TRANSPOSED_OUTPUT;
+}
+
+// offset within the 256-element block -> (rr, cc)
+__device__ __forceinline__ void offset_to_rc(int32_t order, int o, int &rr, int &cc) {
+  const int outer = o >> 4, inner0 = o & 15;
+  const int inner = swizzled(order) ? unswz(inner0) : inner0;
+  if (rows_outer(order)) { rr = outer; cc = inner; } else { cc = outer; rr = inner; }
+}
+
+template <bool kFromRow, bool kToRow>
+__global__ void __launch_bounds__(256) convert_blocks_kernel(Side src, Side dst, int64_t logical_rows,
+                                                             int64_t logical_cols, int64_t matrices) {
+  __shared__ uint16_t tile[8][16][17];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bR = (dst.rows + 15) / 16, bC = (dst.cols + 15) / 16;
+  const int64_t total = matrices * bR * bC;
+  const int64_t vr = min(logical_rows, src.rows), vc = min(logical_cols, src.cols);
+  const uint16_t *sp = static_cast<const uint16_t *>(src.ptr);
+  uint16_t *dp = static_cast<uint16_t *>(dst.ptr);
+  for (int64_t blk = (int64_t)blockIdx.x * 8 + warp; blk < total; blk += (int64_t)gridDim.x * 8) {
+    const int64_t m = blk / (bR * bC);
+    const int64_t rem = blk % (bR * bC);
+    const int64_t br = rem / bC, bc = rem % bC;
+    const int64_t r0 = br * 16, c0 = bc * 16;
+    // ---- gather the source block into tile[warp][rr][cc] ----
+    uint16_t vals[8];
+    int rrs[8], ccs[8];
+    if (kFromRow) {
+      const int rr = lane >> 1, cb0 = (lane & 1) * 8;
+      const int64_t r = r0 + rr;
+      const uint16_t *row = sp + m * src.mstride + r * src.ld + c0 + cb0;
+      const bool full = (r < vr) && (c0 + cb0 + 8 <= vc);
+      if (full && src.vec) {
+        uint4 v = *reinterpret_cast<const uint4 *>(row);
+        const uint16_t *pv = reinterpret_cast<const uint16_t *>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vals[i] = pv[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vals[i] = (r < vr && c0 + cb0 + i < vc) ? row[i] : (uint16_t)0;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { rrs[i] = rr; ccs[i] = cb0 + i; }
+    } else {
+      const int64_t base = m * src.mstride + block_base(src, br, bc);
+      bool all = true;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        offset_to_rc(src.order, lane * 8 + i, rrs[i], ccs[i]);
+        all = all && (r0 + rrs[i] < vr) && (c0 + ccs[i] < vc);
+      }
+      if (all) {
+        uint4 v = *reinterpret_cast<const uint4 *>(sp + base + lane * 8);
+        const uint16_t *pv = reinterpret_cast<const uint16_t *>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vals[i] = pv[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const bool ok = (r0 + rrs[i] < vr) && (c0 + ccs[i] < vc);
+          vals[i] = ok ? sp[base + lane * 8 + i] : (uint16_t)0;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tile[warp][rrs[i]][ccs[i]] = vals[i];
+    __syncwarp();
+    // ---- scatter the destination block ----
+    if (kToRow) {
+      const int rr = lane >> 1, cb0 = (lane & 1) * 8;
+      const int64_t r = r0 + rr;
+      uint16_t *row = dp + m * dst.mstride + r * dst.ld + c0 + cb0;
+      if (r < dst.rows) {
+        if (dst.vec && c0 + cb0 + 8 <= dst.cols) {
+          uint4 v;
+          uint16_t *pv = reinterpret_cast<uint16_t *>(&v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pv[i] = tile[warp][rr][cb0 + i];
+          *reinterpret_cast<uint4 *>(row) = v;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (c0 + cb0 + i < dst.cols) row[i] = tile[warp][rr][cb0 + i];
+        }
+      }
+    } else {
+      const int64_t base = m * dst.mstride + block_base(dst, br, bc);
+      uint16_t out[8];
+      bool all = true;
+      bool ok[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        int rr, cc;
+        offset_to_rc(dst.order, lane * 8 + i, rr, cc);
+        ok[i] = (r0 + rr < dst.rows) && (c0 + cc < dst.cols);
+        all = all && ok[i];
+        out[i] = tile[warp][rr][cc];
+      }
+      if (all) {
+        uint4 v;
+        uint16_t *pv = reinterpret_cast<uint16_t *>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pv[i] = out[i];
+        *reinterpret_cast<uint4 *>(dp + base + lane * 8) = v;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (ok[i]) dp[base + lane * 8 + i] = out[i];
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Host-side geometry checks for a packed side (the divisibility rules of
+// storage.rs: AmpBlock / BlockMajorBlock errors).
+ipuc_status check_side(const Side &s, const char *which) {
+  std::string w(which);
+  switch (s.order) {
+    case IPUC_ORDER_ROW_MAJOR:
+      IPUC_CHECK_ARG(s.ld >= s.cols, w + ": leading dimension smaller than columns");
+      return IPUC_OK;
+    case IPUC_ORDER_AMP_LEFT:
+    case IPUC_ORDER_AMP_OUTPUT:
+      IPUC_CHECK_ARG(s.cols % 16 == 0, w + ": AMP-Left/Output need physical columns % 16 == 0");
+      return IPUC_OK;
+    case IPUC_ORDER_AMP_TRANSPOSED_LEFT:
+    case IPUC_ORDER_AMP_TRANSPOSED_OUTPUT:
+      IPUC_CHECK_ARG(s.rows % 16 == 0, w + ": transposed AMP orders need physical rows % 16 == 0");
+      return IPUC_OK;
+    case IPUC_ORDER_AMP_TRANSPOSED_RIGHT:
+      IPUC_CHECK_ARG(s.rows % 16 == 0 && s.cols % 16 == 0,
+                     w + ": AMP-TransposedRight needs rows % 16 == 0 and columns % 16 == 0");
+      return IPUC_OK;
+    case IPUC_ORDER_BLOCK_MAJOR:
+      IPUC_CHECK_ARG(s.rb > 0 && s.cb > 0 && s.rb % 16 == 0 && s.rows % s.rb == 0 && s.cols % s.cb == 0,
+                     w + ": block-major needs row_block % 16 == 0, rows % row_block == 0, columns % column_block == 0");
+      if (s.cb % 16 != 0) return fail(IPUC_ERR_UNSUPPORTED, w + ": block-major column_block must be a multiple of 16");
+      return IPUC_OK;
+    case IPUC_ORDER_BLOCK_MAJOR_TRANSPOSED:
+      IPUC_CHECK_ARG(s.rb > 0 && s.cb > 0 && s.rb % 16 == 0 && s.cols % s.rb == 0 && s.rows % s.cb == 0,
+                     w + ": transposed block-major needs row_block % 16 == 0, columns % row_block == 0, rows % column_block == 0");
+      if (s.cb % 16 != 0) return fail(IPUC_ERR_UNSUPPORTED, w + ": block-major column_block must be a multiple of 16");
+      return IPUC_OK;
+  }
+  return fail(IPUC_ERR_INVALID_ARGUMENT, w + ": unknown element order");
+}
+
+ipuc_status launch_convert(Side src, Side dst, int64_t logical_rows, int64_t logical_cols, int64_t matrices,
+                           cudaStream_t stream) {
+  ipuc_status st = check_side(src, "source");
+  if (st != IPUC_OK) return st;
+  st = check_side(dst, "destination");
+  if (st != IPUC_OK) return st;
+  IPUC_CHECK_ALIGN(aligned(src.ptr, 16) && aligned(dst.ptr, 16), "rearrange: pointers must be 16-byte aligned");
+  if (src.order != IPUC_ORDER_ROW_MAJOR) IPUC_CHECK_ALIGN(src.mstride % 8 == 0, "rearrange: packed matrix size must be a multiple of 8 elements");
+  if (dst.order != IPUC_ORDER_ROW_MAJOR) IPUC_CHECK_ALIGN(dst.mstride % 8 == 0, "rearrange: packed matrix size must be a multiple of 8 elements");
+  src.vec = (src.ld % 8 == 0 && src.mstride % 8 == 0) ? 1 : 0;
+  dst.vec = (dst.ld % 8 == 0 && dst.mstride % 8 == 0) ? 1 : 0;
+  const int64_t blocks = matrices * ((dst.rows + 15) / 16) * ((dst.cols + 15) / 16);
+  if (blocks == 0) return IPUC_OK;
+  const int64_t want = (blocks + 7) / 8;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  const bool fr = src.order == IPUC_ORDER_ROW_MAJOR, tr = dst.order == IPUC_ORDER_ROW_MAJOR;
+  if (fr && tr) convert_blocks_kernel<true, true><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
+  else if (fr) convert_blocks_kernel<true, false><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
+  else if (tr) convert_blocks_kernel<false, true><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
+  else convert_blocks_kernel<false, false><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
+  return check_launch("convert_blocks_kernel");
+}
+
+// SplitHeads [b, r, h*c] -> [b*h, r, c]: one 8-element chunk per thread.
+template <bool kVec>
+__global__ void split_heads_kernel(uint16_t *__restrict__ out, const uint16_t *__restrict__ in, int64_t batch,
+                                   int64_t rows, int64_t heads, int64_t channels) {
+  const int64_t total = batch * heads * rows * channels;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * 8;
+  for (int64_t o = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; o < total; o += step) {
+    if (kVec) {
+      const int64_t c = o % channels, t = o / channels, r = t % rows, bh = t / rows;
+      const int64_t b = bh / heads, h = bh % heads;
+      const int64_t s = (b * rows + r) * heads * channels + h * channels + c;
+      *reinterpret_cast<uint4 *>(out + o) = *reinterpret_cast<const uint4 *>(in + s);
+    } else {
+      for (int64_t e = o; e < o + 8 && e < total; ++e) {
+        const int64_t c = e % channels, t = e / channels, r = t % rows, bh = t / rows;
+        const int64_t b = bh / heads, h = bh % heads;
+        out[e] = in[(b * rows + r) * heads * channels + h * channels + c];
+      }
+    }
+  }
+}
+
+}  // namespace
+}  // namespace ipuc
+
+using namespace ipuc;
+
+extern "C" ipuc_status ipuc_rearrange_f16(void *dst, const void *src, int64_t matrices, int64_t logical_rows,
+                                          int64_t physical_rows, int32_t target_order, int64_t logical_columns,
+                                          int64_t physical_columns, int64_t row_block, int64_t column_block,
+                                          ipuc_stream stream) {
+  IPUC_CHECK_ARG(matrices >= 0 && logical_rows >= 0 && logical_columns >= 0, "rearrange: negative extent");
+  IPUC_CHECK_ARG(logical_rows <= physical_rows && logical_columns <= physical_columns,
+                 "rearrange: logical extent exceeds physical extent");
+  IPUC_CHECK_ARG(logical_columns % 2 == 0, "rearrange: logical columns must be even (rearrange_f16.cpp:34)");
+  IPUC_CHECK_ARG(physical_columns % 16 == 0, "rearrange: physical columns must be a multiple of 16");
+  int32_t order;
+  switch (target_order) {
+    case 0: order = IPUC_ORDER_AMP_LEFT; break;
+    case 1:
+      order = IPUC_ORDER_AMP_TRANSPOSED_RIGHT;
+      if (column_block != 16) return fail(IPUC_ERR_UNSUPPORTED, "rearrange: AMP-TransposedRight supports 16-row panels");
+      break;
+    case 2: order = IPUC_ORDER_BLOCK_MAJOR; break;
+    default: return fail(IPUC_ERR_INVALID_ARGUMENT, "rearrange: target_order must be 0, 1 or 2");
+  }
+  if (matrices == 0 || physical_rows == 0) return IPUC_OK;
+  Side s{const_cast<void *>(src), IPUC_ORDER_ROW_MAJOR, logical_rows, logical_columns, logical_columns,
+         logical_rows * logical_columns, 0, 0, 0};
+  Side d{dst, order, physical_rows, physical_columns, physical_columns, physical_rows * physical_columns,
+         row_block, column_block, 0};
+  return launch_convert(s, d, logical_rows, logical_columns, matrices, stream);
+}
+
+extern "C" ipuc_status ipuc_unpack_f16(void *dst, const void *src, int32_t source_order, int64_t matrices,
+                                       int64_t logical_rows, int64_t physical_rows, int64_t logical_columns,
+                                       int64_t physical_columns, ipuc_stream stream) {
+  IPUC_CHECK_ARG(matrices >= 0 && logical_rows >= 0 && logical_columns >= 0, "unpack: negative extent");
+  IPUC_CHECK_ARG(logical_rows <= physical_rows && logical_columns <= physical_columns,
+                 "unpack: logical extent exceeds physical extent");
+  IPUC_CHECK_ARG(physical_columns % 2 == 0, "unpack: physical columns must be even (unpack_amp_f16.cpp:31)");
+  int32_t order;
+  if (source_order == 0) order = IPUC_ORDER_AMP_OUTPUT;
+  else if (source_order == 1) order = IPUC_ORDER_AMP_TRANSPOSED_LEFT;
+  else return fail(IPUC_ERR_INVALID_ARGUMENT, "unpack: source_order must be 0 (AMP-Output) or 1 (AMP-TransposedLeft)");
+  if (matrices == 0 || physical_rows == 0) return IPUC_OK;
+  const int64_t me = physical_rows * physical_columns;
+  Side s{const_cast<void *>(src), order, physical_rows, physical_columns, physical_columns, me, 0, 0, 0};
+  Side d{dst, IPUC_ORDER_ROW_MAJOR, physical_rows, physical_columns, physical_columns, me, 0, 0, 0};
+  return launch_convert(s, d, logical_rows, logical_columns, matrices, stream);
+}
+
+extern "C" ipuc_status ipuc_convert_order_f16(void *dst, ipuc_order to, const void *src, ipuc_order from,
+                                              int64_t matrices, int64_t rows, int64_t columns, int64_t row_block,
+                                              int64_t column_block, ipuc_stream stream) {
+  IPUC_CHECK_ARG(matrices >= 0 && rows >= 0 && columns >= 0, "convert_order: negative extent");
+  if (matrices == 0 || rows == 0 || columns == 0) return IPUC_OK;
+  const int64_t me = rows * columns;
+  Side s{const_cast<void *>(src), (int32_t)from, rows, columns, columns, me, row_block, column_block, 0};
+  Side d{dst, (int32_t)to, rows, columns, columns, me, row_block, column_block, 0};
+  return launch_convert(s, d, rows, columns, matrices, stream);
+}
+
+extern "C" ipuc_status ipuc_split_heads_f16(void *out, const void *in, int64_t batch, int64_t rows, int64_t heads,
+                                            int64_t channels, ipuc_stream stream) {
+  IPUC_CHECK_ARG(batch >= 0 && rows >= 0 && heads > 0 && channels > 0, "split_heads: bad extents");
+  const int64_t total = batch * rows * heads * channels;
+  if (total == 0) return IPUC_OK;
+  const bool vec = channels % 8 == 0 && aligned(out, 16) && aligned(in, 16);
+  const int64_t chunks = (total + 7) / 8;
+  const int64_t want = (chunks + 255) / 256, cap = (int64_t)sm_count() * 16;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  if (vec)
+    split_heads_kernel<true><<<grid, 256, 0, stream>>>((uint16_t *)out, (const uint16_t *)in, batch, rows, heads, channels);
+  else
+    split_heads_kernel<false><<<grid, 256, 0, stream>>>((uint16_t *)out, (const uint16_t *)in, batch, rows, heads, channels);
+  return check_launch("split_heads_kernel");
+}

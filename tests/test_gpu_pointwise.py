@@ -1,0 +1,80 @@
+"""Parity of GELU, reduce_add, Add and Cast against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import ipuc
+import oracle
+from conftest import f16_close, seeded_normal
+from gpu_util import dev_f32, dev_u16, empty_u16, f16_of, host_f32, host_u16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("n", [2, 6, 8, 1000, 1 << 20, (1 << 20) + 6])
+def test_gelu_f16(n):
+    x = oracle.f16_bits(seeded_normal(n, n, 3.0))
+    want = oracle.gelu_f16_bits(x)
+    out = empty_u16(n)
+    ipuc.gelu_f16(out, dev_u16(x))
+    got = host_u16(out)
+    ok, msg = f16_close(f16_of(got), f16_of(want))
+    assert ok, msg
+    # tanh via exp identity: at most 1 ulp from the f32 tanhf formula
+    assert (np.abs(got.astype(np.int32) - want.astype(np.int32)) <= 1).all()
+    assert (got == want).mean() > 0.99
+
+
+def test_gelu_in_place_and_extremes():
+    x = np.array([0.0, -0.0, 1.0, -1.0, 10.0, -10.0, 65504.0, -65504.0], np.float32)
+    xb = oracle.f16_bits(x)
+    t = dev_u16(xb)
+    ipuc.gelu_f16(t, t)
+    got = f16_of(host_u16(t))
+    want = f16_of(oracle.gelu_f16_bits(xb))
+    assert np.allclose(got, want, atol=1e-3, equal_nan=False)
+
+
+@pytest.mark.parametrize("prec", [ipuc.F16, ipuc.F32])
+@pytest.mark.parametrize("partials,n", [(2, 8), (4, 4096), (4, 1 << 20), (7, 8 * 1000)])
+def test_reduce_sum(prec, partials, n):
+    p = seeded_normal(partials * 31 + n, (partials, n), 2.0)
+    if prec == ipuc.F16:
+        pb = oracle.f16_bits(p)
+        want = oracle.reduce_sum(pb[0], pb[1:])
+        initial, remote = dev_u16(pb[0]), dev_u16(pb[1:])
+    else:
+        want = oracle.reduce_sum(p[0], p[1:])
+        initial, remote = dev_f32(p[0]), dev_f32(p[1:])
+    out = empty_u16(n)
+    ipuc.reduce_sum(out, initial, remote, partials - 1, n, prec)
+    got = host_u16(out)
+    # f32 accumulation of the same values in the same order: bit-exact
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n,lp,rp", [(4096, 0, 0), (4096, 0, 64), (1000, 0, 10), (77, 7, 0)])
+def test_add_f16(n, lp, rp):
+    l = oracle.f16_bits(seeded_normal(1, lp or n))
+    r = oracle.f16_bits(seeded_normal(2, rp or n))
+    want = oracle.add_f16(l, r, n, lp, rp)
+    out = empty_u16(n)
+    ipuc.add_f16(out, dev_u16(l), dev_u16(r), n, lp, rp)
+    assert np.array_equal(host_u16(out), want)
+
+
+def test_cast_round_trip():
+    x = seeded_normal(3, 5000, 100.0)
+    xd = dev_f32(x)
+    h = empty_u16(5000)
+    ipuc.cast(h, ipuc.F16, xd, ipuc.F32, 5000)
+    assert np.array_equal(host_u16(h), oracle.f16_bits(x))
+    back = torch.empty(5000, dtype=torch.float32, device="cuda")
+    ipuc.cast(back, ipuc.F32, h, ipuc.F16, 5000)
+    assert np.array_equal(host_f32(back), oracle.quantize_f16(x))
+
+
+def test_fill_zero():
+    t = empty_u16(4096)
+    ipuc.fill_zero(t)
+    assert (host_u16(t) == 0).all()
