@@ -1,0 +1,343 @@
+// Fused non-causal flash attention on the tcgen05 tensor cores: the B200
+// counterpart of flash_attention_online_f16 (device/flash_attention_online_f16.
+// cpp:61-143) and of the reference's four-launches-per-key-block staged loop
+// (crates/ipu-codegen/src/low.rs:2272-2510: QK^T GEMM -> softmax -> PV GEMM ->
+// merge, with the exact online max/denominator recurrence of
+// device/attention_stages_f16.S:803-849).
+//
+// One CTA owns 256 query rows of one stream as two 128-row tiles (Q0, Q1) and
+// streams 128-key K/V tiles through a 2-stage TMA ring.  Warp roles:
+//   warp 0      TMA loads (Q once; K_j, V_j per key tile)
+//   warp 1      MMA issue: S_t = Q_t K_j^T into TMEM, then O_t += P_t V_j with
+//               P_t read straight from TMEM (it aliases S_t as packed f16)
+//   warps 2-5   softmax for Q0; warps 6-9 softmax for Q1 (thread = query row)
+// The two tiles ping-pong so the tensor core computes one tile's products
+// while the other tile's softmax runs.  TMEM: S0 | S1 | O0 | O1 (4 x 128 cols).
+// The softmax keeps an fp32 running max and denominator per row; the O rescale
+// (the merge stage's acc*e^{m-m'}) is applied only when a row's max grows by
+// more than 2^8 in the exponent, which keeps P <= 256 and is exact because
+// the final 1/denominator uses the same stale max.
+// Head dims up to 128 (multiple of 8) are zero-padded to 128 by the TMA; key
+// and query tails are masked.  Every wait is bounded (error word, no trap).
+#include <math.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
+
+namespace ipuc {
+namespace {
+
+using namespace sm100;
+
+constexpr int TQ = 128;       // query rows per tile
+constexpr int TK = 128;       // keys per tile
+constexpr int DP = 128;       // padded head dim
+constexpr int TILE_BYTES = TQ * DP * 2;   // 32 KB (two 16 KB swizzled halves)
+constexpr int HALF_BYTES = TILE_BYTES / 2;
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr int NUM_THREADS = 320;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+struct AttnParams {
+  void *out;
+  int64_t matrices, sq, sk, d;
+  float scale_log2;  // softmax scale * log2(e)
+  int32_t out_f32;
+  int32_t key_tiles;
+  uint32_t *err;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sQ = smem;                       // Q0, Q1
+  uint8_t *sK = smem + 2 * TILE_BYTES;      // 2 stages
+  uint8_t *sV = smem + 4 * TILE_BYTES;      // 2 stages
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * TILE_BYTES);
+  uint64_t *q_full = bars + 0;
+  uint64_t *k_full = bars + 1;   // [2]
+  uint64_t *v_full = bars + 3;   // [2]
+  uint64_t *kv_empty = bars + 5; // [2]
+  uint64_t *s_full = bars + 7;   // [2] per Q tile
+  uint64_t *p_ready = bars + 9;  // [2] per Q tile
+  uint64_t *o_final = bars + 11;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t stream = blockIdx.y;
+  const int32_t q0 = blockIdx.x * (2 * TQ);
+  const int n_tiles = p.key_tiles;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], 128);
+    }
+    mbar_init(o_final, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S_t at t*128, O_t at 256 + t*128.
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * TQ, (int32_t)stream);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait_bounded(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sK + st * TILE_BYTES + h * HALF_BYTES, &tmK, &k_full[st], h * 64, j * TK, (int32_t)stream);
+        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, j * TK, (int32_t)stream);
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_PRODUCER);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc(TQ, TK, 0, false, false);  // K-major Q and K
+      constexpr uint32_t idesc_o = make_idesc(TQ, DP, 0, false, true);   // V is MN-major (D contiguous)
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      auto issue_s = [&](int t, int stage) {
+        const uint32_t qa = q_addr + t * TILE_BYTES, ka = k_addr + stage * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < DP / 16; ++k) {
+          const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
+          mma_f16_ss(tmem + t * 128, make_smem_desc(qa + off, 16, 1024, kSwizzle128B),
+                     make_smem_desc(ka + off, 16, 1024, kSwizzle128B), idesc_s, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[t]);
+      };
+      if (ok) ok = mbar_wait_bounded(&k_full[0], 0, abort_flag);
+      if (ok) {
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait_bounded(&v_full[st], (j >> 1) & 1, abort_flag)) { ok = false; break; }
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!mbar_wait_bounded(&p_ready[t], j & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t va = v_addr + st * TILE_BYTES;
+#pragma unroll
+          for (int k = 0; k < TK / 16; ++k) {
+            // A = P_t (f16, 8 TMEM columns per 16 keys); B = V rows [16k, 16k+16)
+            mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8,
+                       make_smem_desc(va + k * 2048, HALF_BYTES, 1024, kSwizzle128B), idesc_o,
+                       (j > 0 || k > 0) ? 1u : 0u);
+          }
+          if (j + 1 < n_tiles) {
+            const int nst = (j + 1) & 1;
+            if (t == 0 && !mbar_wait_bounded(&k_full[nst], ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+            issue_s(t, nst);
+          }
+        }
+        mma_commit(&kv_empty[st]);
+      }
+      if (ok) mma_commit(o_final);
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_MMA);
+        *abort_flag = 1;
+      }
+    }
+  } else {
+    // Softmax warpgroups: t = 0 for warps 2-5, 1 for warps 6-9.
+    const int t = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + t * 128;
+    const uint32_t o_col = tmem + lane_off + 256 + t * 128;
+    const float c = p.scale_log2;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      // Pass 1: row max over the valid keys of this tile (S stays in TMEM).
+      const int64_t rem_keys = p.sk - (int64_t)j * TK;
+      const int valid = rem_keys < TK ? (int)rem_keys : TK;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int ch = 0; ch < TK / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(s_col + ch * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (ch * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      const float m_new = fmaxf(m, mx);
+      bool rescale = false;
+      float alpha = 1.0f;
+      if (j == 0) {
+        m = m_new;
+      } else if ((m_new - m) * c > RESCALE_THRESHOLD) {
+        alpha = ex2_approx((m - m_new) * c);
+        rescale = true;
+        m = m_new;
+        l *= alpha;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_t is stable: PV_t(j-1) was issued before S_t(j), whose completion we observed.
+#pragma unroll
+        for (int ch = 0; ch < DP / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(o_col + ch * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x32(o_col + ch * 32, r);
+        }
+      }
+      const float mc = m * c;
+      float sum = 0.0f;
+      // Pass 2: P = 2^(s*c - m*c) as packed f16, written over the first 64 columns of S.
+#pragma unroll
+      for (int ch = 0; ch < TK / 64; ++ch) {
+        uint32_t a[32], b[32];
+        tmem_ld_32x32b_x32(s_col + ch * 64, a);
+        tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
+        tmem_wait_ld();
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = ch * 64 + 2 * i;
+          const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
+          const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
+          const float p0 = col < valid ? ex2_approx(fmaf(x0, c, -mc)) : 0.0f;
+          const float p1 = col + 1 < valid ? ex2_approx(fmaf(x1, c, -mc)) : 0.0f;
+          sum += p0 + p1;
+          __half2 h2 = __floats2half2_rn(p0, p1);
+          packed[i] = *reinterpret_cast<uint32_t *>(&h2);
+        }
+        tmem_st_32x32b_x32(s_col + ch * 32, packed);
+      }
+      l += sum;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[t]);
+    }
+    // Epilogue: O_t / l -> out.
+    if (ok && mbar_wait_bounded(o_final, 0, abort_flag)) {
+      tc_fence_after();
+      const int64_t row = (int64_t)q0 + t * TQ + quarter * 32 + lane;
+      const float inv = 1.0f / l;
+      const bool row_ok = row < p.sq;
+      const int64_t base = (stream * p.sq + row) * p.d;
+#pragma unroll
+      for (int ch = 0; ch < DP / 32; ++ch) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_col + ch * 32, r);
+        tmem_wait_ld();
+        if (!row_ok || ch * 32 >= p.d) continue;
+        if (p.out_f32) {
+          float *o = static_cast<float *>(p.out) + base + ch * 32;
+          for (int i = 0; i < 32 && ch * 32 + i < p.d; i += 4)
+            *reinterpret_cast<float4 *>(o + i) =
+                make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                            __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+        } else {
+          uint16_t *o = static_cast<uint16_t *>(p.out) + base + ch * 32;
+          for (int i = 0; i < 32 && ch * 32 + i < p.d; i += 8) {
+            uint4 v;
+            v.x = pack_h2(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv);
+            v.y = pack_h2(__uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+            v.z = pack_h2(__uint_as_float(r[i + 4]) * inv, __uint_as_float(r[i + 5]) * inv);
+            v.w = pack_h2(__uint_as_float(r[i + 6]) * inv, __uint_as_float(r[i + 7]) * inv);
+            *reinterpret_cast<uint4 *>(o + i) = v;
+          }
+        }
+      }
+    } else if (ok) {
+      ok = false;
+    }
+    if (!ok) {
+      record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_EPILOGUE);
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+}  // namespace ipuc
+
+using namespace ipuc;
+
+extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_precision, const void *q, const void *k,
+                                                const void *v, int64_t matrices, int64_t query_rows, int64_t key_rows,
+                                                int64_t head_dim, float scale, ipuc_stream stream) {
+  IPUC_CHECK_ARG(out_precision == IPUC_F16 || out_precision == IPUC_F32, "flash_attention: bad output precision");
+  IPUC_CHECK_ARG(matrices >= 0 && query_rows >= 0 && key_rows >= 0, "flash_attention: negative extent");
+  if (matrices == 0 || query_rows == 0) return IPUC_OK;
+  IPUC_CHECK_ARG(key_rows > 0, "flash_attention: key rows must be positive");
+  IPUC_CHECK_ARG(head_dim > 0 && head_dim % 8 == 0, "flash_attention: head_dim must be a positive multiple of 8");
+  if (head_dim > 128) return fail(IPUC_ERR_UNSUPPORTED, "flash_attention: head_dim above 128 is not supported");
+  IPUC_CHECK_ARG(out && q && k && v, "flash_attention: null pointer");
+  IPUC_CHECK_ALIGN(aligned(out, 16) && aligned(q, 16) && aligned(k, 16) && aligned(v, 16),
+                   "flash_attention: pointers must be 16-byte aligned");
+  IPUC_CHECK_ARG(matrices < 65536 && query_rows < (1ll << 31) && key_rows < (1ll << 31),
+                 "flash_attention: extent too large");
+  CUtensorMap tq, tk, tv;
+  ipuc_status st = make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q, head_dim, query_rows, matrices, head_dim,
+                               query_rows * head_dim, 64, TQ);
+  if (st != IPUC_OK) return st;
+  st = make_map_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, k, head_dim, key_rows, matrices, head_dim,
+                   key_rows * head_dim, 64, TK);
+  if (st != IPUC_OK) return st;
+  st = make_map_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v, head_dim, key_rows, matrices, head_dim,
+                   key_rows * head_dim, 64, TK);
+  if (st != IPUC_OK) return st;
+  AttnParams p;
+  p.out = out;
+  p.matrices = matrices;
+  p.sq = query_rows;
+  p.sk = key_rows;
+  p.d = head_dim;
+  const float s = scale > 0.0f ? scale : 1.0f / sqrtf((float)head_dim);
+  p.scale_log2 = s * 1.4426950408889634f;
+  p.out_f32 = out_precision == IPUC_F32;
+  p.key_tiles = (int32_t)((key_rows + TK - 1) / TK);
+  p.err = device_error_word();
+  IPUC_CUDA(cudaFuncSetAttribute(flash_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  dim3 grid((unsigned)((query_rows + 2 * TQ - 1) / (2 * TQ)), (unsigned)matrices);
+  flash_attention_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  return check_launch("flash_attention_kernel");
+}

@@ -9,7 +9,3 @@ extern "C" ipuc_status ipuc_gemm_f32(float *, const float *, const float *, int6
                                      int64_t, int64_t, uint32_t, void *, uint64_t, ipuc_stream) {
   return fail(IPUC_ERR_UNSUPPORTED, "gemm_f32: not built");
 }
-extern "C" ipuc_status ipuc_flash_attention_f16(void *, ipuc_precision, const void *, const void *, const void *,
-                                                int64_t, int64_t, int64_t, int64_t, float, ipuc_stream) {
-  return fail(IPUC_ERR_UNSUPPORTED, "flash_attention: not built");
-}
