@@ -1,0 +1,513 @@
+"""Benchmark of the B200 operator-catalog hot path (one JSON line on rank 0).
+
+Headline step (BASELINE.json metric "FP16 GEMM & flash-attn TFLOP/s"):
+  * config 3  MLP up-projection: X[8192x4096] f16 ~N(0,1) times
+    W[4096x16384] f16 ~N(0,1/4096), tanh-GELU fused into the GEMM epilogue,
+    f16 out (ipuc_gemm_f16 with IPUC_GEMM_EPILOGUE_GELU);
+  * config 4  flash attention: 8 x 32 streams, S=4096, D=128, Q/K/V ~N(0,1)
+    f16, scale 1/sqrt(128), f16 out (ipuc_flash_attention_f16).
+With N GPUs the GEMM is sharded along N (columns of W) and attention along
+batch x heads (strong scaling: the total work is fixed); outputs stay sharded,
+so no collective sits in the step.  value = algorithmic FLOP of the whole
+step (1.0995e12 + 2.1990e12) / max-over-ranks device time.
+
+Timing: W warm-up steps, then K timed steps bracketed by barrier +
+synchronize, CUDA events on the launching stream.  Inputs (0.45 GB GEMM,
+1 GB attention per step) exceed the 126 MB L2, so no flush is needed.
+
+--impl reference times the reference's CPU evaluation of the same step on the
+host cores (the oracle restatement of crates/ipu-tests/src/diagnostic.rs:
+OpenBLAS SGEMM + scalar GELU, scalar attention loop) on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ipu-stack_b200"))
+
+# ---- workload constants (BASELINE.json configs 3 and 4) ---------------------
+MLP_M, MLP_K, MLP_N = 8192, 4096, 16384
+ATT_B, ATT_H, ATT_S, ATT_D = 8, 32, 4096, 128
+GEMM_FLOP = 2.0 * MLP_M * MLP_N * MLP_K                      # 1.0995e12
+ATT_FLOP = 4.0 * ATT_B * ATT_H * ATT_S * ATT_S * ATT_D        # 2.1990e12
+STEP_FLOP = GEMM_FLOP + ATT_FLOP
+REARRANGE_ROWS, REARRANGE_COLS = 4096, 49152                  # 201M elements: config-5 weight tiles
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p.get("bf16_tflops", 1590.0), p.get("bf16_tflops_sustained", 1400.0), p.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def setup_dist(want_gpus: int):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def shard(total: int, world: int, rank: int):
+    base = total // world
+    return rank * base, base if rank < world - 1 else total - base * (world - 1)
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import ipuc
+
+    rank, world, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream()
+    s = stream.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+
+    n0, nw = shard(MLP_N, world, rank)
+    s0, ns = shard(ATT_B * ATT_H, world, rank)
+    x = torch.randn((MLP_M, MLP_K), generator=g, device=dev, dtype=torch.float32).half()
+    w = (torch.randn((MLP_K, nw), generator=g, device=dev, dtype=torch.float32) * (1.0 / 64.0)).half()
+    y = torch.empty((MLP_M, nw), device=dev, dtype=torch.float16)
+    q = torch.randn((ns, ATT_S, ATT_D), generator=g, device=dev, dtype=torch.float32).half()
+    k = torch.randn((ns, ATT_S, ATT_D), generator=g, device=dev, dtype=torch.float32).half()
+    v = torch.randn((ns, ATT_S, ATT_D), generator=g, device=dev, dtype=torch.float32).half()
+    o = torch.empty((ns, ATT_S, ATT_D), device=dev, dtype=torch.float16)
+
+    def gemm():
+        ipuc.call("ipuc_gemm_f16", y.data_ptr(), x.data_ptr(), w.data_ptr(), MLP_M, nw, MLP_K, MLP_K, nw, nw,
+                  ipuc.GEMM_EPILOGUE_GELU, s)
+
+    def attn():
+        ipuc.call("ipuc_flash_attention_f16", o.data_ptr(), ipuc.F16, q.data_ptr(), k.data_ptr(), v.data_ptr(), ns,
+                  ATT_S, ATT_S, ATT_D, 0.0, s)
+
+    def step():
+        gemm()
+        attn()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- headline timed region ----
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
+    ev[0].record(stream)
+    for i in range(args.steps):
+        gemm()
+        ev[2 * i + 1].record(stream)
+        attn()
+        ev[2 * i + 2].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop()
+    total_ms = ev[0].elapsed_time(ev[-1])
+    gemm_ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps
+    attn_ms = sum(ev[2 * i + 1].elapsed_time(ev[2 * i + 2]) for i in range(args.steps)) / args.steps
+    ipuc.device_status(stream)
+    total_ms = max_over_ranks(total_ms, world)
+    gemm_ms = max_over_ranks(gemm_ms, world)
+    attn_ms = max_over_ranks(attn_ms, world)
+    ms_per_step = total_ms / args.steps
+    value = STEP_FLOP / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the C ABI with host buffers ----
+    pin = lambda t: torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    hx, hw, hq, hk, hv = pin(x), pin(w), pin(q), pin(k), pin(v)
+    hy, ho = pin(y), pin(o)
+    for h, d in ((hx, x), (hw, w), (hq, q), (hk, k), (hv, v)):
+        h.copy_(d)
+    torch.cuda.synchronize()
+
+    def e2e_step():
+        x.copy_(hx, non_blocking=True)
+        w.copy_(hw, non_blocking=True)
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        gemm()
+        attn()
+        hy.copy_(y, non_blocking=True)
+        ho.copy_(o, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    h2d = sum(t.numel() * t.element_size() for t in (hx, hw, hq, hk, hv))
+    d2h = sum(t.numel() * t.element_size() for t in (hy, ho))
+
+    # ---- supplementary components (not in value) ----
+    comps = {}
+    peak_burst, peak_sus, hbm, peak_kind = load_peaks()
+    if rank == 0:
+        comps = measure_components(ipuc, torch, stream, hbm)
+
+    # ---- CPU baseline (oracle, bounded sample, rank 0 at N=1) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        dom = "flash_attention" if attn_ms >= gemm_ms else "gemm_f16_gelu"
+        dom_ms = attn_ms if dom == "flash_attention" else gemm_ms
+        dom_flop = (ATT_FLOP * ns / (ATT_B * ATT_H)) if dom == "flash_attention" else (GEMM_FLOP * nw / MLP_N)
+        achieved = dom_flop / (dom_ms * 1e-3) / 1e12
+        line = {
+            "metric": "FP16 GEMM (MLP up-proj, fused GELU) + flash-attention TFLOP/s",
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) / N(0,1/4096) f16, BASELINE shapes)",
+            "config": {"workload": "config3 MLP up-proj 8192x4096x16384 +GELU fused, N-sharded; config4 flash "
+                                   "attention B=8 H=32 S=4096 D=128, sharded over batch*heads",
+                       "global_batch": MLP_M, "seq_len": ATT_S, "parallelism": f"shard{world}",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clock_info,
+            "e2e": {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1), "peak": peak_sus,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak_sus, 4),
+                         "peak_kind": f"{peak_kind} bf16 sustained", "frac_of_burst": round(achieved / peak_burst, 4),
+                         "traffic": profiled_traffic(dom)},
+            "kernels": {"gemm_f16_gelu": {"ms": round(gemm_ms, 4),
+                                          "tflops": round(GEMM_FLOP * nw / MLP_N / (gemm_ms * 1e-3) / 1e12, 1)},
+                        "flash_attention": {"ms": round(attn_ms, 4),
+                                            "tflops": round(ATT_FLOP * ns / (ATT_B * ATT_H) / (attn_ms * 1e-3) / 1e12, 1)}},
+            "components": comps,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get(kernel)
+    return None
+
+
+def measure_components(ipuc, torch, stream, hbm_gbs):
+    """Rearrange GB/s (config-5 weight tiles) and FP32 GEMM TFLOP/s (config 2),
+    reported beside the headline, not folded into it."""
+    s = stream.cuda_stream
+    out = {}
+    # row-major -> block-major {64,16}, 201M f16 elements
+    n = REARRANGE_ROWS * REARRANGE_COLS
+    src = torch.empty(n, dtype=torch.int16, device="cuda").random_(-30000, 30000)
+    dst = torch.empty(n, dtype=torch.int16, device="cuda")
+    for target in (0, 2):
+        def run():
+            ipuc.call("ipuc_rearrange_f16", dst.data_ptr(), src.data_ptr(), 1, REARRANGE_ROWS, REARRANGE_ROWS, target,
+                      REARRANGE_COLS, REARRANGE_COLS, 64, 16, s)
+        for _ in range(3):
+            run()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(stream)
+        for _ in range(10):
+            run()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 10
+        gbs = 2 * n * 2 / (ms * 1e-3) / 1e9
+        out[f"rearrange_{'amp_left' if target == 0 else 'block_major'}"] = {
+            "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3)}
+    del src, dst
+    # FP32 GEMM 4096^3 (3xTF32)
+    try:
+        m = n_ = k = 4096
+        a32 = torch.rand((m, k), device="cuda") * 2 - 1
+        b32 = torch.rand((k, n_), device="cuda") * 2 - 1
+        c32 = torch.empty((m, n_), device="cuda")
+        ws = torch.empty(max(1, ipuc.gemm_f32_workspace_bytes(m, n_, k)), dtype=torch.uint8, device="cuda")
+
+        def run32():
+            ipuc.call("ipuc_gemm_f32", c32.data_ptr(), a32.data_ptr(), b32.data_ptr(), m, n_, k, k, n_, n_, 0,
+                      ws.data_ptr(), ws.numel(), s)
+        for _ in range(3):
+            run32()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(stream)
+        for _ in range(10):
+            run32()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 10
+        out["gemm_f32_4096"] = {"ms": round(ms, 4), "tflops": round(2 * m * n_ * k / (ms * 1e-3) / 1e12, 1)}
+    except ipuc.IpucError as e:
+        out["gemm_f32_4096"] = {"unavailable": str(e)}
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle = restatement of the reference's host evaluator)
+# ---------------------------------------------------------------------------
+
+class CpuSample:
+    """The reference CPU path on a bounded sample of the step, scaled to the
+    full step: GEMM+GELU on R rows of X against all of W (f32 OpenBLAS SGEMM on
+    f16-quantised values, f16 rounding of each op result), and the scalar
+    attention loop on `streams` streams x Sq query rows against all 4096 keys."""
+
+    R, SQ = 1024, 64
+
+    def __init__(self, threads: int):
+        import numpy as np
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        self.oracle = oracle
+        self.threads = threads
+        rng = np.random.default_rng(0)
+        self.xs = oracle.quantize_f16(rng.standard_normal((self.R, MLP_K), dtype=np.float32))
+        self.ws = oracle.quantize_f16(rng.standard_normal((MLP_K, MLP_N), dtype=np.float32) / 64)
+        self.streams = max(1, threads)
+        shape_q, shape_kv = (self.streams, self.SQ, ATT_D), (self.streams, ATT_S, ATT_D)
+        self.q = oracle.quantize_f16(rng.standard_normal(shape_q, dtype=np.float32))
+        self.k = oracle.quantize_f16(rng.standard_normal(shape_kv, dtype=np.float32))
+        self.v = oracle.quantize_f16(rng.standard_normal(shape_kv, dtype=np.float32))
+
+    def run(self):
+        o = self.oracle
+        t0 = time.perf_counter()
+        y = o.quantize_f16(o.gemm(self.xs, self.ws))
+        o.quantize_f16(o.gelu(y))
+        t_gemm = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        o.attention(self.q, self.k, self.v, threads=self.threads)
+        t_att = time.perf_counter() - t0
+        gemm_full = t_gemm * (MLP_M / self.R)
+        att_full = t_att * (ATT_B * ATT_H * ATT_S) / (self.streams * self.SQ)
+        tflops = STEP_FLOP / (gemm_full + att_full) / 1e12
+        sample = (f"GEMM+GELU on {self.R} of {MLP_M} rows ({t_gemm:.2f} s, OpenBLAS, {self.threads} threads); "
+                  f"attention {self.streams} streams x {self.SQ} of {ATT_S} query rows ({t_att:.2f} s, "
+                  f"{self.threads} threads); scaled linearly to the full step ({gemm_full + att_full:.0f} s)")
+        return tflops, sample
+
+
+def cpu_baseline(seconds_budget: float):
+    threads = os.cpu_count() or 1
+    cs = CpuSample(threads)
+    cs.run()  # warm the BLAS thread pool
+    tflops, sample = cs.run()
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    sample = ""
+    cs = CpuSample(threads)
+    for _ in range(max(1, min(args.warmup, 2))):
+        cs.run()  # warm-up (BLAS thread pool, page faults)
+    for _ in range(min(args.steps, 10)):
+        tf, sample = cs.run()
+        vals.append(tf)
+    value = statistics.median(vals)
+    line = {
+        "metric": "FP16 GEMM (MLP up-proj, fused GELU) + flash-attention TFLOP/s",
+        "impl": "reference",
+        "value": round(value, 6),
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(STEP_FLOP / (value * 1e12) * 1e3, 1),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 (f16-quantised operands)",
+        "data": "synthetic",
+        "config": {"workload": "config3 MLP up-proj + config4 flash attention (reference host evaluator on CPU)"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def profile_case(kernel: str):
+    """Small single-kernel cases for ncu: inputs above the 126 MB L2 but a few
+    hundred MB on the device in total; 1 warm-up + 3 launches."""
+    import torch
+    import ipuc
+    torch.cuda.set_device(0)
+    s = torch.cuda.current_stream().cuda_stream
+    if kernel == "gemm":
+        m, n, k = 4096, 8192, 4096
+        a = torch.randn((m, k), device="cuda").half()
+        b = (torch.randn((k, n), device="cuda") / 64).half()
+        c = torch.empty((m, n), device="cuda", dtype=torch.float16)
+        run = lambda: ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n,
+                                ipuc.GEMM_EPILOGUE_GELU, s)
+    elif kernel == "attention":
+        M = 32
+        q, kk, v = (torch.randn((M, ATT_S, ATT_D), device="cuda").half() for _ in range(3))
+        o = torch.empty_like(q)
+        run = lambda: ipuc.call("ipuc_flash_attention_f16", o.data_ptr(), ipuc.F16, q.data_ptr(), kk.data_ptr(),
+                                v.data_ptr(), M, ATT_S, ATT_S, ATT_D, 0.0, s)
+    elif kernel == "rearrange":
+        rows, cols = 4096, 16384
+        src = torch.empty(rows * cols, dtype=torch.int16, device="cuda").random_(-30000, 30000)
+        dst = torch.empty_like(src)
+        run = lambda: ipuc.call("ipuc_rearrange_f16", dst.data_ptr(), src.data_ptr(), 1, rows, rows, 2, cols, cols,
+                                64, 16, s)
+    else:
+        m = n = k = 4096
+        a = torch.rand((m, k), device="cuda")
+        b = torch.rand((k, n), device="cuda")
+        c = torch.empty((m, n), device="cuda")
+        ws = torch.empty(max(1, ipuc.gemm_f32_workspace_bytes(m, n, k)), dtype=torch.uint8, device="cuda")
+        run = lambda: ipuc.call("ipuc_gemm_f32", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, 0,
+                                ws.data_ptr(), ws.numel(), s)
+    for _ in range(4):
+        run()
+    torch.cuda.synchronize()
+    ipuc.device_status()
+    print(f"profile case {kernel}: ok")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--profile", choices=["gemm", "attention", "rearrange", "gemm_f32"],
+                    help="run a few launches of one kernel on a small case (for ncu captures) and exit")
+    args = ap.parse_args()
+    if args.profile:
+        profile_case(args.profile)
+        return
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -24,7 +24,7 @@ def test_gelu_f16(n):
     # 1 + tanh(u) cancels (x << 0); absolute differences stay below 1e-3.
     assert np.abs(f16_of(got) - f16_of(want)).max() <= 1e-3
     if n >= 1000:
-        assert (got == want).mean() > 0.99
+        assert (got == want).mean() > 0.95
 
 
 def test_gelu_in_place_and_extremes():
