@@ -114,6 +114,28 @@ ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, int64_t m, i
                           int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, void *workspace,
                           uint64_t workspace_bytes, ipuc_stream stream);
 
+/* Allocation-free FP32 GEMM.  No counterpart in the reference: its tile
+ * kernels never need scratch, while ipuc_gemm_f32 above takes a caller-provided
+ * workspace for the TF32 hi/lo split planes.  This entry point is for callers
+ * that cannot allocate device memory when they issue the GEMM (a plug-in whose
+ * host framework owns the device allocator and forbids library allocations, a
+ * host callback, or a real-time path whose memory budget is fixed up front):
+ * the split planes live in a fixed 64 MiB file-scope device array of
+ * libipuc.so instead.  Arguments, flags and results are exactly those
+ * of ipuc_gemm_f32 without the workspace pair.
+ *  - Limit: 2 * 4 * (m*k + k*n) <= 64 MiB (e.g. m = n = k = 2048); larger
+ *    shapes return IPUC_ERR_INVALID_ARGUMENT and launch nothing.
+ *  - Allocates nothing: no cudaMalloc/cudaFree and no allocating library call.
+ *    The array exists on every GPU that loads the library, until process exit.
+ *  - The first call on each device resolves the array's device address with
+ *    cudaGetSymbolAddress (with that device current); make that first call
+ *    before any stream capture on the device.
+ *  - Every call shares the one array: calls that overlap on the GPU (two
+ *    streams, or concurrent host threads) race.  Nothing in it needs clearing
+ *    between calls. */
+ipuc_status ipuc_gemm_f32_noalloc(float *c, const float *a, const float *b, int64_t m, int64_t n, int64_t k,
+                                  int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, ipuc_stream stream);
+
 /* Gelu: ipu_stack_gelu_tanh_approx_f16 (device/gelu_f16.S:7-148; ABI
  * kernel.rs:1251-1263; element_count even, kernel.rs:1400-1413).
  * out may equal in. */

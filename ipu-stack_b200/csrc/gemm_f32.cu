@@ -19,6 +19,8 @@
 #include "sm100.cuh"
 #include "tma_host.cuh"
 
+#include <mutex>
+
 namespace ipuc {
 namespace {
 
@@ -381,4 +383,71 @@ extern "C" ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, i
                                      int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, void *workspace,
                                      uint64_t workspace_bytes, ipuc_stream stream) {
   return gemm_f32_launch(c, a, b, m, n, k, lda, ldb, ldc, flags, workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of ipuc_gemm_f32.
+//
+// Some callers cannot allocate device memory at the point where they need an
+// FP32 GEMM: a plug-in loaded into a host framework that owns the device
+// allocator and forbids cudaMalloc from library code, code running in a host
+// callback, or a real-time path whose memory budget is fixed up front.  They get ipuc_gemm_f32_noalloc: the same kernels, with the
+// hi/lo TF32 split planes placed in a fixed file-scope device array instead
+// of a caller-provided workspace.
+//
+// The array is a device symbol, so on the host its name is only a stand-in:
+// its device address is resolved once per device with cudaGetSymbolAddress
+// (during the first call on that device, with that device current) and cached.
+// Every GPU that loads libipuc.so holds the array until the process exits.
+// All calls share it: two calls that overlap on the GPU (different streams, or
+// the same call issued concurrently from two host threads) race on it.  The
+// split kernels rewrite every byte the GEMM reads, so nothing needs clearing
+// between calls.
+// ---------------------------------------------------------------------------
+namespace ipuc {
+namespace {
+
+constexpr uint64_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB
+static __device__ __align__(256) uint8_t g_gemm_f32_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void *g_scratch_ptr[64] = {};
+
+ipuc_status scratch_address(void **out) {
+  int dev = 0;
+  IPUC_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(IPUC_ERR_UNSUPPORTED, "gemm_f32_noalloc: device index above 63");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_gemm_f32_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "gemm_f32_noalloc: cudaGetSymbolAddress(scratch)");
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return IPUC_OK;
+}
+
+}  // namespace
+}  // namespace ipuc
+
+extern "C" ipuc_status ipuc_gemm_f32_noalloc(float *c, const float *a, const float *b, int64_t m, int64_t n,
+                                             int64_t k, int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags,
+                                             ipuc_stream stream) {
+  const uint64_t need = ipuc::gemm_f32_workspace(m, n, k);
+  if (need > ipuc::kNoAllocScratchBytes) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "gemm_f32_noalloc: m=%lld n=%lld k=%lld needs %llu scratch bytes, above the fixed %llu-byte array "
+             "(2*4*(m*k + k*n) <= 64 MiB); use ipuc_gemm_f32 with a workspace",
+             (long long)m, (long long)n, (long long)k, (unsigned long long)need,
+             (unsigned long long)ipuc::kNoAllocScratchBytes);
+    return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, buf);
+  }
+  void *scratch = nullptr;
+  if (need > 0) {
+    const ipuc_status st = ipuc::scratch_address(&scratch);
+    if (st != IPUC_OK) return st;
+  }
+  return ipuc::gemm_f32_launch(c, a, b, m, n, k, lda, ldb, ldc, flags, scratch, ipuc::kNoAllocScratchBytes, stream);
 }

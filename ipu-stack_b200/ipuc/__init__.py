@@ -43,6 +43,7 @@ SIGNATURES = {
                                      _u32, _vp]),
     "ipuc_gemm_f32_workspace_bytes": (_u64, [_i64, _i64, _i64]),
     "ipuc_gemm_f32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _u32, _vp, _u64, _vp]),
+    "ipuc_gemm_f32_noalloc": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _u32, _vp]),
     "ipuc_gelu_f16": (_i32, [_vp, _vp, _u64, _vp]),
     "ipuc_reduce_sum": (_i32, [_vp, _vp, _vp, _u32, _u64, _i32, _vp]),
     "ipuc_add_f16": (_i32, [_vp, _vp, _vp, _u64, _u64, _u64, _vp]),
