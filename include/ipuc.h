@@ -82,8 +82,9 @@ ipuc_status ipuc_fill_zero(void *out, uint64_t bytes, ipuc_stream stream);
  * A row-major (lda >= k).  B row-major [k x n] (ldb >= n), or with
  * IPUC_GEMM_B_TRANSPOSED stored as [n x k] (ldb >= k).  C row-major (ldc >= n),
  * f16, or f32 with IPUC_GEMM_OUT_F32 (split-K partials).  fp32 accumulation
- * over the whole k in tensor memory.  Requirements: k % 64 == 0,
- * m, n >= 1, 16-byte aligned pointers, lda/ldb/ldc multiples of 8 elements.
+ * over the whole k in tensor memory.  Requirements: 16-byte aligned
+ * pointers; k, lda and ldb multiples of 8 elements (16-byte TMA rows).  Any
+ * m, n >= 0 (tails are masked); stores are vectorised when ldc % 8 == 0.
  * Epilogue order: acc (+C) -> round to C's precision -> GELU -> store.
  * mode Accumulate == IPUC_GEMM_ACCUMULATE (GemmKernelMode, operator.rs:98-102). */
 enum {
@@ -107,8 +108,9 @@ ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t
  * 129-385).  f32 in, f32 out, C (+)= A.B with three-pass TF32 splitting on the
  * tensor cores (hi.hi + hi.lo + lo.hi), accurate to an f32 tolerance.
  * workspace: caller-provided device scratch of ipuc_gemm_f32_workspace_bytes()
- * bytes (the hi/lo split operands), 256-byte aligned.  Requirements as
- * ipuc_gemm_f16 except k % 32 == 0 and lda/ldb/ldc multiples of 4. */
+ * bytes (the hi/lo split operands), 256-byte aligned.  Requirements:
+ * 16-byte aligned pointers; k, n, lda and ldb multiples of 4 elements.
+ * Flags: IPUC_GEMM_ACCUMULATE and IPUC_GEMM_B_TRANSPOSED. */
 uint64_t ipuc_gemm_f32_workspace_bytes(int64_t m, int64_t n, int64_t k);
 ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, int64_t m, int64_t n, int64_t k,
                           int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, void *workspace,
@@ -168,8 +170,9 @@ ipuc_status ipuc_cast(void *out, ipuc_precision to, const void *in, ipuc_precisi
  *   V [matrices][key_rows][head_dim] f16 row-major; out [matrices][query_rows]
  *   [head_dim] in out_precision (F32 = the reference vertex; F16 = BASELINE).
  * scale <= 0 selects 1/sqrt(head_dim) (AttentionScale::InverseSqrtQueryWidth).
- * fp32 running max/denominator.  head_dim == 128 (tensor-core path) or
- * head_dim % 8 == 0 && head_dim <= 256 (general path). */
+ * fp32 running max/denominator.  head_dim % 8 == 0 and head_dim <= 128
+ * (smaller head dims are zero-padded to 128 inside the kernel); larger head
+ * dims return IPUC_ERR_UNSUPPORTED.  Any query/key row counts >= 1. */
 ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_precision, const void *q,
                                      const void *k, const void *v, int64_t matrices,
                                      int64_t query_rows, int64_t key_rows, int64_t head_dim,
