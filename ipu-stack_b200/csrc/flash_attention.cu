@@ -188,15 +188,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Pass 1: row max over the valid keys of this tile (S stays in TMEM).
       const int64_t rem_keys = p.sk - (int64_t)j * TK;
       const int valid = rem_keys < TK ? (int)rem_keys : TK;
+      const bool full_tile = valid == TK;
       float mx = -INFINITY;
+      if (full_tile) {
+        float mx1 = -INFINITY;
 #pragma unroll
-      for (int ch = 0; ch < TK / 32; ++ch) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(s_col + ch * 32, r);
-        tmem_wait_ld();
+        for (int ch = 0; ch < TK / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(s_col + ch * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (ch * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+          for (int i = 0; i < 32; i += 4) {
+            mx = max3(mx, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+            mx1 = max3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          }
+        }
+        mx = fmaxf(mx, mx1);
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < TK / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(s_col + ch * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (ch * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        }
       }
       const float m_new = fmaxf(m, mx);
       bool rescale = false;
@@ -223,26 +240,64 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       const float mc = m * c;
       float sum = 0.0f;
-      // Pass 2: P = 2^(s*c - m*c) as packed f16, written over the first 64 columns of S.
+      // Pass 2: P = 2^(s*c - m*c) as packed f16, written over the first 64
+      // columns of S.  Full tiles use packed f32x2 arithmetic and compute one
+      // pair in four on the FMA pipe (exp2_poly2) to unload the MUFU unit.
+      if (full_tile) {
+        const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
+        uint64_t sum2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
-      for (int ch = 0; ch < TK / 64; ++ch) {
-        uint32_t a[32], b[32];
-        tmem_ld_32x32b_x32(s_col + ch * 64, a);
-        tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
-        tmem_wait_ld();
-        uint32_t packed[32];
+        for (int ch = 0; ch < TK / 64; ++ch) {
+          uint32_t a[32], b[32];
+          tmem_ld_32x32b_x32(s_col + ch * 64, a);
+          tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
+          tmem_wait_ld();
+          uint32_t packed[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = ch * 64 + 2 * i;
-          const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
-          const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
-          const float p0 = col < valid ? ex2_approx(fmaf(x0, c, -mc)) : 0.0f;
-          const float p1 = col + 1 < valid ? ex2_approx(fmaf(x1, c, -mc)) : 0.0f;
-          sum += p0 + p1;
-          __half2 h2 = __floats2half2_rn(p0, p1);
-          packed[i] = *reinterpret_cast<uint32_t *>(&h2);
+          for (int i = 0; i < 32; ++i) {
+            const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
+            const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
+            const uint64_t t = f2_fma(f2_pack(x0, x1), c2, nmc2);
+            uint64_t pp;
+            if ((i & 3) == 3) {
+              pp = exp2_poly2(t);
+            } else {
+              float t0, t1;
+              f2_unpack(t, t0, t1);
+              pp = f2_pack(ex2_approx(t0), ex2_approx(t1));
+            }
+            sum2 = f2_add(sum2, pp);
+            float p0, p1;
+            f2_unpack(pp, p0, p1);
+            __half2 h2 = __floats2half2_rn(p0, p1);
+            packed[i] = *reinterpret_cast<uint32_t *>(&h2);
+          }
+          tmem_st_32x32b_x32(s_col + ch * 32, packed);
         }
-        tmem_st_32x32b_x32(s_col + ch * 32, packed);
+        float s0, s1;
+        f2_unpack(sum2, s0, s1);
+        sum = s0 + s1;
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < TK / 64; ++ch) {
+          uint32_t a[32], b[32];
+          tmem_ld_32x32b_x32(s_col + ch * 64, a);
+          tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
+          tmem_wait_ld();
+          uint32_t packed[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = ch * 64 + 2 * i;
+            const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
+            const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
+            const float p0 = col < valid ? ex2_approx(fmaf(x0, c, -mc)) : 0.0f;
+            const float p1 = col + 1 < valid ? ex2_approx(fmaf(x1, c, -mc)) : 0.0f;
+            sum += p0 + p1;
+            __half2 h2 = __floats2half2_rn(p0, p1);
+            packed[i] = *reinterpret_cast<uint32_t *>(&h2);
+          }
+          tmem_st_32x32b_x32(s_col + ch * 32, packed);
+        }
       }
       l += sum;
       tmem_wait_st();
