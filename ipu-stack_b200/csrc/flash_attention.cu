@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int ch = 0; ch < TK / 32; ++ch) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(s_col + ch * 32, r);
-          tmem_wait_ld();
+          tmem_wait_ld(r);
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             mx = max3(mx, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int ch = 0; ch < TK / 32; ++ch) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(s_col + ch * 32, r);
-          tmem_wait_ld();
+          tmem_wait_ld(r);
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (ch * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int ch = 0; ch < DP / 32; ++ch) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(o_col + ch * 32, r);
-          tmem_wait_ld();
+          tmem_wait_ld(r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           tmem_st_32x32b_x32(o_col + ch * 32, r);
@@ -251,7 +251,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t a[32], b[32];
           tmem_ld_32x32b_x32(s_col + ch * 64, a);
           tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
-          tmem_wait_ld();
+          tmem_wait_ld(a);
+          tmem_regs_fence(b);
           uint32_t packed[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -283,7 +284,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint32_t a[32], b[32];
           tmem_ld_32x32b_x32(s_col + ch * 64, a);
           tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
-          tmem_wait_ld();
+          tmem_wait_ld(a);
+          tmem_regs_fence(b);
           uint32_t packed[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int ch = 0; ch < DP / 32; ++ch) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(o_col + ch * 32, r);
-        tmem_wait_ld();
+        tmem_wait_ld(r);
         if (!row_ok || ch * 32 >= p.d) continue;
         if (p.out_f32) {
           float *o = static_cast<float *>(p.out) + base + ch * 32;

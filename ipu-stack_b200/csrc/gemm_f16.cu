@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + buf * BN + chunk * 32 + ((uint32_t)(quarter * 32) << 16), r);
-        tmem_wait_ld();
+        tmem_wait_ld(r);
         const int64_t col0 = (int64_t)nt * BN + chunk * 32;
         if (!row_ok || col0 >= p.n) continue;
         const bool full_chunk = vec_ok && (col0 + 32 <= p.n);

@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int ch = 0; ch < BN / 64; ++ch) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + buf * BN + half * (BN / 2) + ch * 32 + ((uint32_t)(quarter * 32) << 16), r);
-          tmem_wait_ld();
+          tmem_wait_ld(r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) acc[ch * 32 + i] += __uint_as_float(r[i]);
         }

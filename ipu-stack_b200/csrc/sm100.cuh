@@ -171,6 +171,24 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// tcgen05.ld writes its destination registers asynchronously until
+// tcgen05.wait::ld, but the compiler sees them as defined at the load and may
+// schedule arithmetic on them above the wait.  After the wait, every loaded
+// register passes through this empty volatile asm, which "redefines" it after
+// the wait in program order, so no use can move above it.
+__device__ __forceinline__ void tmem_regs_fence(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  tmem_wait_ld();
+  tmem_regs_fence(r);
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 2^x on the MUFU unit (PTX ex2.approx.ftz.f32).
@@ -209,12 +227,14 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // n = round(t) (the 1.5*2^23 shifter) and f in [-0.5, 0.5]; 2^f is a degree-3
 // polynomial fitted here by weighted least squares (max relative error
 // 7.5e-5, below half an f16 ulp), and 2^n is added to the exponent field.
-// Inputs are clamped at -127 so the exponent arithmetic cannot wrap.
+// Inputs are clamped at -125: with 2^f in [0.70, 1.42] the exponent field
+// then stays in [1, 254], so adding n to it can neither wrap nor underflow
+// (2^-125 rounds to 0 in the f16 P anyway).
 __device__ __forceinline__ uint64_t exp2_poly2(uint64_t t) {
   float t0, t1;
   f2_unpack(t, t0, t1);
-  t0 = fmaxf(t0, -127.0f);
-  t1 = fmaxf(t1, -127.0f);
+  t0 = fmaxf(t0, -125.0f);
+  t1 = fmaxf(t1, -125.0f);
   const uint64_t shifter = f2_pack(12582912.0f, 12582912.0f);
   const uint64_t tt = f2_pack(t0, t1);
   const uint64_t y = f2_add(tt, shifter);                      // round(t) in the low mantissa bits
