@@ -194,6 +194,161 @@ __global__ void __launch_bounds__(256) convert_blocks_kernel(Side src, Side dst,
   }
 }
 
+// Same conversion with 32-bit index arithmetic inside a matrix (used when a
+// matrix holds fewer than 2^31 elements): every CTA of 8 warps owns 8
+// consecutive micro-blocks of one 16-row band, so the work index is divided
+// once per CTA, and each lane's in-block permutation (which depends only on the
+// order and the lane) is computed once per thread, not once per block.
+__device__ __forceinline__ int32_t block_base32(const Side &s, int32_t br, int32_t bc) {
+  const int32_t R = (int32_t)s.rows, C = (int32_t)s.cols;
+  switch (s.order) {
+    case IPUC_ORDER_AMP_LEFT:
+    case IPUC_ORDER_AMP_OUTPUT:
+      return bc * R * 16 + br * 256;
+    case IPUC_ORDER_AMP_TRANSPOSED_LEFT:
+    case IPUC_ORDER_AMP_TRANSPOSED_OUTPUT:
+      return br * C * 16 + bc * 256;
+    case IPUC_ORDER_AMP_TRANSPOSED_RIGHT:
+      return (br * (C >> 4) + bc) * 256;
+    case IPUC_ORDER_BLOCK_MAJOR: {
+      const int32_t rb = (int32_t)s.rb, cb = (int32_t)s.cb, r0 = br * 16, c0 = bc * 16, rg = rb >> 4;
+      const int32_t panel = (r0 / rb) * (C / cb) * rg + (c0 / cb) * rg + (r0 % rb) / 16;
+      return panel * 16 * cb + (c0 % cb) * 16;
+    }
+    case IPUC_ORDER_BLOCK_MAJOR_TRANSPOSED: {
+      const int32_t rb = (int32_t)s.rb, cb = (int32_t)s.cb, r0 = bc * 16, c0 = br * 16, rg = rb >> 4;
+      const int32_t panel = (r0 / rb) * (R / cb) * rg + (c0 / cb) * rg + (r0 % rb) / 16;
+      return panel * 16 * cb + (c0 % cb) * 16;
+    }
+  }
+  return 0;
+}
+
+constexpr int kBlocksPerWarp = 4;  // loads of 4 micro-blocks in flight per warp
+
+template <bool kFromRow, bool kToRow>
+__device__ __forceinline__ void lane_rc(const Side &s, bool row_major, int lane, int i, int &rr, int &cc) {
+  if (row_major) { rr = lane >> 1; cc = (lane & 1) * 8 + i; }
+  else offset_to_rc(s.order, lane * 8 + i, rr, cc);
+}
+
+// kMode: 0 = general in-block permutation through shared memory;
+//        1 = source and destination place every lane's 8 elements at the same
+//            in-block coordinates (rows-outer orders and row-major, or two
+//            columns-outer orders): the 16-byte chunk passes straight through;
+//        2 = one side rows-outer, the other columns-outer: a 16x16 transpose
+//            through a padded tile written with 8-byte stores.
+template <bool kFromRow, bool kToRow, int kMode>
+__global__ void __launch_bounds__(256, 4) convert_blocks32_kernel(Side src, Side dst, int32_t logical_rows,
+                                                                  int32_t logical_cols, int32_t matrices) {
+  __shared__ __align__(16) uint16_t tile[8][16 * 20];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kSpan = 8 * kBlocksPerWarp;  // micro-blocks per CTA work item
+  const int32_t bR = (int32_t)((dst.rows + 15) / 16), bC = (int32_t)((dst.cols + 15) / 16);
+  const int32_t groups = (bC + kSpan - 1) / kSpan;
+  const uint32_t total = (uint32_t)matrices * (uint32_t)bR * (uint32_t)groups;
+  const int32_t vr = min(logical_rows, (int32_t)src.rows), vc = min(logical_cols, (int32_t)src.cols);
+  const int32_t drows = (int32_t)dst.rows, dcols = (int32_t)dst.cols;
+  const uint16_t *sp = static_cast<const uint16_t *>(src.ptr);
+  uint16_t *dp = static_cast<uint16_t *>(dst.ptr);
+  // Per-lane shared-memory slots (rr*17 + cc) of the 8 elements this lane
+  // moves, two 16-bit slots per register, and the extreme in-block row and
+  // column (for the whole-chunk bounds test).
+  uint32_t sslot[4], dslot[4];
+  int smax_r = 0, smax_c = 0, dmax_r = 0, dmax_c = 0;
+  int srow0 = 0, scol0 = 0, drow0 = 0, dcol0 = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int rr, cc;
+    lane_rc<kFromRow, kToRow>(src, kFromRow, lane, i, rr, cc);
+    if (i == 0) { srow0 = rr; scol0 = cc; }
+    smax_r = max(smax_r, rr); smax_c = max(smax_c, cc);
+    const uint32_t sv = (uint32_t)(rr * 17 + cc);
+    sslot[i >> 1] = (i & 1) ? (sslot[i >> 1] | (sv << 16)) : sv;
+    lane_rc<kFromRow, kToRow>(dst, kToRow, lane, i, rr, cc);
+    if (i == 0) { drow0 = rr; dcol0 = cc; }
+    dmax_r = max(dmax_r, rr); dmax_c = max(dmax_c, cc);
+    const uint32_t dv = (uint32_t)(rr * 17 + cc);
+    dslot[i >> 1] = (i & 1) ? (dslot[i >> 1] | (dv << 16)) : dv;
+  }
+  uint16_t *t = tile[warp];
+  for (uint32_t w = blockIdx.x; w < total; w += gridDim.x) {
+    const uint32_t per_m = (uint32_t)bR * (uint32_t)groups;
+    const int32_t m = (int32_t)(w / per_m);
+    const uint32_t rem = w - (uint32_t)m * per_m;
+    const int32_t br = (int32_t)(rem / (uint32_t)groups);
+    const int32_t bc0 = (int32_t)(rem - (uint32_t)br * (uint32_t)groups) * kSpan + warp;
+    const int32_t r0 = br * 16;
+    const uint16_t *sbase = sp + (int64_t)m * src.mstride;
+    uint16_t *dbase = dp + (int64_t)m * dst.mstride;
+    uint4 v[kBlocksPerWarp];
+    // Issue all loads first so kBlocksPerWarp 16-byte reads per lane are in flight.
+#pragma unroll
+    for (int u = 0; u < kBlocksPerWarp; ++u) {
+      const int32_t bc = bc0 + 8 * u, c0 = bc * 16;
+      if (bc >= bC) continue;  // warp-uniform
+      const int32_t soff = kFromRow ? (r0 + srow0) * (int32_t)src.ld + c0 + scol0 : block_base32(src, br, bc) + lane * 8;
+      if ((r0 + smax_r < vr) && (c0 + smax_c < vc) && (kFromRow ? src.vec != 0 : true)) {
+        v[u] = *reinterpret_cast<const uint4 *>(sbase + soff);
+      } else {
+        uint16_t *pv = reinterpret_cast<uint16_t *>(&v[u]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          int rr, cc;
+          lane_rc<kFromRow, kToRow>(src, kFromRow, lane, i, rr, cc);
+          pv[i] = (r0 + rr < vr && c0 + cc < vc) ? sbase[soff + i] : (uint16_t)0;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlocksPerWarp; ++u) {
+      const int32_t bc = bc0 + 8 * u, c0 = bc * 16;
+      if (bc >= bC) continue;
+      uint4 o;
+      if (kMode == 1) {
+        o = v[u];
+      } else if (kMode == 2) {
+        // Lane l holds element i of line l/2 at position 8(l%2)+i; it writes
+        // the line (row stride 20 halves keeps the column reads conflict-free)
+        // and reads back line positions as columns.
+        uint2 *w2 = reinterpret_cast<uint2 *>(t + (lane >> 1) * 20 + (lane & 1) * 8);
+        w2[0] = make_uint2(v[u].x, v[u].y);
+        w2[1] = make_uint2(v[u].z, v[u].w);
+        __syncwarp();
+        uint32_t *po = reinterpret_cast<uint32_t *>(&o);
+        const uint16_t *col = t + ((lane & 1) * 8) * 20 + (lane >> 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) po[j] = (uint32_t)col[(2 * j) * 20] | ((uint32_t)col[(2 * j + 1) * 20] << 16);
+        __syncwarp();
+      } else {
+        const uint32_t *pv = reinterpret_cast<const uint32_t *>(&v[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[sslot[j] & 0xffffu] = (uint16_t)(pv[j] & 0xffffu);
+          t[sslot[j] >> 16] = (uint16_t)(pv[j] >> 16);
+        }
+        __syncwarp();
+        uint32_t *po = reinterpret_cast<uint32_t *>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) po[j] = (uint32_t)t[dslot[j] & 0xffffu] | ((uint32_t)t[dslot[j] >> 16] << 16);
+        __syncwarp();
+      }
+      const int32_t doff = kToRow ? (r0 + drow0) * (int32_t)dst.ld + c0 + dcol0 : block_base32(dst, br, bc) + lane * 8;
+      if ((r0 + dmax_r < drows) && (c0 + dmax_c < dcols) && (kToRow ? dst.vec != 0 : true)) {
+        *reinterpret_cast<uint4 *>(dbase + doff) = o;
+      } else {
+        const uint16_t *ph = reinterpret_cast<const uint16_t *>(&o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          int rr, cc;
+          lane_rc<kFromRow, kToRow>(dst, kToRow, lane, i, rr, cc);
+          if (r0 + rr < drows && c0 + cc < dcols) dbase[doff + i] = ph[i];
+        }
+      }
+    }
+  }
+}
+
 // Host-side geometry checks for a packed side (the divisibility rules of
 // storage.rs: AmpBlock / BlockMajorBlock errors).
 ipuc_status check_side(const Side &s, const char *which) {
@@ -241,10 +396,45 @@ ipuc_status launch_convert(Side src, Side dst, int64_t logical_rows, int64_t log
   dst.vec = (dst.ld % 8 == 0 && dst.mstride % 8 == 0) ? 1 : 0;
   const int64_t blocks = matrices * ((dst.rows + 15) / 16) * ((dst.cols + 15) / 16);
   if (blocks == 0) return IPUC_OK;
+  const bool fr = src.order == IPUC_ORDER_ROW_MAJOR, tr = dst.order == IPUC_ORDER_ROW_MAJOR;
+  const int64_t lim = (int64_t)1 << 30;
+  const int64_t work32 = matrices * ((dst.rows + 15) / 16) * (((dst.cols + 15) / 16 + 8 * kBlocksPerWarp - 1) / (8 * kBlocksPerWarp));
+  if (src.mstride < lim && dst.mstride < lim && src.rows * src.ld < lim && dst.rows * dst.ld < lim &&
+      dst.rows * dst.cols + 4096 < lim && src.rows * src.cols + 4096 < lim && work32 < lim && matrices < lim) {
+    const int64_t cap = (int64_t)sm_count() * 8;
+    const unsigned grid = (unsigned)(work32 < cap ? work32 : cap);
+    const int32_t lr = (int32_t)(logical_rows < lim ? logical_rows : lim);
+    const int32_t lc = (int32_t)(logical_cols < lim ? logical_cols : lim);
+    // In-block lane layout of each side: 0 rows-outer, 1 columns-outer, 2 swizzled.
+    auto kind = [](int32_t o) {
+      switch (o) {
+        case IPUC_ORDER_ROW_MAJOR: case IPUC_ORDER_AMP_LEFT: case IPUC_ORDER_AMP_TRANSPOSED_RIGHT:
+        case IPUC_ORDER_BLOCK_MAJOR_TRANSPOSED: return 0;
+        case IPUC_ORDER_AMP_TRANSPOSED_LEFT: case IPUC_ORDER_BLOCK_MAJOR: return 1;
+        default: return 2;
+      }
+    };
+    const int ks = kind(src.order), kd = kind(dst.order);
+    const int mode = (ks == 2 || kd == 2) ? 0 : (ks == kd ? 1 : 2);
+#define IPUC_CONVERT32(FR, TR, MODE) \
+  convert_blocks32_kernel<FR, TR, MODE><<<grid, 256, 0, stream>>>(src, dst, lr, lc, (int32_t)matrices)
+#define IPUC_CONVERT32_MODES(FR, TR)          \
+  do {                                        \
+    if (mode == 1) IPUC_CONVERT32(FR, TR, 1); \
+    else if (mode == 2) IPUC_CONVERT32(FR, TR, 2); \
+    else IPUC_CONVERT32(FR, TR, 0);           \
+  } while (0)
+    if (fr && tr) IPUC_CONVERT32_MODES(true, true);
+    else if (fr) IPUC_CONVERT32_MODES(true, false);
+    else if (tr) IPUC_CONVERT32_MODES(false, true);
+    else IPUC_CONVERT32_MODES(false, false);
+#undef IPUC_CONVERT32_MODES
+#undef IPUC_CONVERT32
+    return check_launch("convert_blocks32_kernel");
+  }
   const int64_t want = (blocks + 7) / 8;
   const int64_t cap = (int64_t)sm_count() * 8;
   const unsigned grid = (unsigned)(want < cap ? want : cap);
-  const bool fr = src.order == IPUC_ORDER_ROW_MAJOR, tr = dst.order == IPUC_ORDER_ROW_MAJOR;
   if (fr && tr) convert_blocks_kernel<true, true><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
   else if (fr) convert_blocks_kernel<true, false><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
   else if (tr) convert_blocks_kernel<false, true><<<grid, 256, 0, stream>>>(src, dst, logical_rows, logical_cols, matrices);
