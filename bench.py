@@ -447,31 +447,32 @@ def run_reference(args):
 
 
 def profile_case(kernel: str):
-    """Small single-kernel cases for ncu: inputs above the 126 MB L2 but a few
-    hundred MB on the device in total; 1 warm-up + 3 launches."""
+    """One kernel at the exact shape the headline step launches it with (at most
+    ~1.3 GB on the device), for ncu captures: 1 warm-up + 3 launches."""
     import torch
     import ipuc
     torch.cuda.set_device(0)
     s = torch.cuda.current_stream().cuda_stream
     if kernel == "gemm":
-        m, n, k = 4096, 8192, 4096
+        m, n, k = MLP_M, MLP_N, MLP_K
         a = torch.randn((m, k), device="cuda").half()
         b = (torch.randn((k, n), device="cuda") / 64).half()
         c = torch.empty((m, n), device="cuda", dtype=torch.float16)
         run = lambda: ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n,
                                 ipuc.GEMM_EPILOGUE_GELU, s)
     elif kernel == "attention":
-        M = 32
+        M = ATT_B * ATT_H
         q, kk, v = (torch.randn((M, ATT_S, ATT_D), device="cuda").half() for _ in range(3))
         o = torch.empty_like(q)
         run = lambda: ipuc.call("ipuc_flash_attention_f16", o.data_ptr(), ipuc.F16, q.data_ptr(), kk.data_ptr(),
                                 v.data_ptr(), M, ATT_S, ATT_S, ATT_D, 0.0, s)
-    elif kernel == "rearrange":
-        rows, cols = 4096, 16384
+    elif kernel in ("rearrange", "rearrange_amp_left"):
+        rows, cols = REARRANGE_ROWS, REARRANGE_COLS
         src = torch.empty(rows * cols, dtype=torch.int16, device="cuda").random_(-30000, 30000)
         dst = torch.empty_like(src)
-        run = lambda: ipuc.call("ipuc_rearrange_f16", dst.data_ptr(), src.data_ptr(), 1, rows, rows, 2, cols, cols,
-                                64, 16, s)
+        target = 2 if kernel == "rearrange" else 0
+        run = lambda: ipuc.call("ipuc_rearrange_f16", dst.data_ptr(), src.data_ptr(), 1, rows, rows, target, cols,
+                                cols, 64, 16, s)
     else:
         m = n = k = 4096
         a = torch.rand((m, k), device="cuda")
@@ -495,7 +496,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
-    ap.add_argument("--profile", choices=["gemm", "attention", "rearrange", "gemm_f32"],
+    ap.add_argument("--profile", choices=["gemm", "attention", "rearrange", "rearrange_amp_left", "gemm_f32"],
                     help="run a few launches of one kernel on a small case (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile:
