@@ -67,6 +67,25 @@ __device__ __forceinline__ float gelu_f32(float x) {
   return x * __frcp_rn(1.0f + e);
 }
 
+// GELU on a pair of f16 values in f16x2 arithmetic, the way the reference's
+// tile kernel evaluates it (device/gelu_f16.S:14-25: f16v2mul/add/tanh):
+// y = x/2 * (1 + tanh(0.7978846 * (x + 0.044715 x^3))), tanh from the
+// hardware tanh.approx.f16x2.  Used by the GEMM epilogue, where the f32
+// formula's extra MUFU work would otherwise dominate.  For |x| large enough
+// that x^3 overflows, tanh saturates to +-1 and the result is x or 0.
+__device__ __forceinline__ uint32_t gelu_h2(uint32_t xh) {
+  const __half2 x = *reinterpret_cast<const __half2 *>(&xh);
+  const __half2 x2 = __hmul2(x, x);
+  const __half2 inner = __hfma2(__hmul2(x2, x), __float2half2_rn(0.044715f), x);
+  const __half2 u = __hmul2(inner, __float2half2_rn(0.7978846f));
+  uint32_t ub = *reinterpret_cast<const uint32_t *>(&u), tb;
+  asm("tanh.approx.f16x2 %0, %1;" : "=r"(tb) : "r"(ub));
+  const __half2 t = *reinterpret_cast<const __half2 *>(&tb);
+  const __half2 hx = __hmul2(x, __float2half2_rn(0.5f));
+  const __half2 y = __hfma2(hx, t, hx);
+  return *reinterpret_cast<const uint32_t *>(&y);
+}
+
 }  // namespace ipuc
 
 #define IPUC_CHECK_ARG(cond, msg)                                   \

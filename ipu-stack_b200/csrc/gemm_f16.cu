@@ -10,7 +10,7 @@
 //               thread, commits stage releases and accumulator-ready signals.
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (each warp owns its
 //               32-lane TMEM quarter), optional accumulate with C, rounding,
-//               fused tanh-GELU, f16 or f32 stores.  Double-buffered TMEM lets
+//               fused tanh-GELU (f16x2, as the reference kernel), f16 or f32 stores.  Double-buffered TMEM lets
 //               the epilogue of tile i overlap the MMAs of tile i+1.
 // The whole K loop accumulates in TMEM (fp32), so the reference's f16 partial
 // round trip between 64-wide K blocks (gemm_f16_amp.S:363-437) disappears.
@@ -54,6 +54,74 @@ __device__ __forceinline__ void tile_coords(const GemmParams &p, int64_t t, int 
   const int64_t w = r % in_group;
   mt = first + (int)(w % gs);
   nt = (int)(w / gs);
+}
+
+// Epilogue for one 32-column chunk of one accumulator row: optional
+// accumulate with C, rounding to C's precision, fused GELU, vector stores.
+__device__ __forceinline__ void store_chunk(const GemmParams &p, int b, int64_t row, int64_t col0,
+                                            const uint32_t (&r)[32], bool vec_ok, bool out_f32, bool accumulate,
+                                            bool gelu) {
+  const bool full_chunk = vec_ok && (col0 + 32 <= p.n);
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (out_f32) {
+    float *cp = static_cast<float *>(p.c) + b * p.stride_c + row * p.ldc + col0;
+    if (full_chunk) {
+      float4 *c4 = reinterpret_cast<float4 *>(cp);
+      if (accumulate) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 o = c4[j];
+          v[4 * j] += o.x; v[4 * j + 1] += o.y; v[4 * j + 2] += o.z; v[4 * j + 3] += o.w;
+        }
+      }
+      if (gelu) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_f32(v[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) c4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+      for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+        float x = v[j];
+        if (accumulate) x += cp[j];
+        if (gelu) x = gelu_f32(x);
+        cp[j] = x;
+      }
+    }
+  } else {
+    uint16_t *cp = static_cast<uint16_t *>(p.c) + b * p.stride_c + row * p.ldc + col0;
+    if (full_chunk) {
+      uint4 *c4 = reinterpret_cast<uint4 *>(cp);
+      if (accumulate) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 o = c4[j];
+          const uint16_t *h = reinterpret_cast<const uint16_t *>(&o);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[8 * j + e] += h2f(h[e]);
+        }
+      }
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        packed[j] = pack_h2(v[2 * j], v[2 * j + 1]);  // the GEMM result rounded to f16
+        if (gelu) packed[j] = gelu_h2(packed[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        c4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+    } else {
+      for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
+        float x = v[j];
+        if (accumulate) x += h2f(cp[j]);
+        uint32_t h = f2h(x);
+        if (gelu) h = gelu_h2(h) & 0xffffu;
+        cp[j] = (uint16_t)h;
+      }
+    }
+  }
 }
 
 template <bool kBKMajor>
@@ -190,70 +258,7 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld(r);
         const int64_t col0 = (int64_t)nt * BN + chunk * 32;
         if (!row_ok || col0 >= p.n) continue;
-        const bool full_chunk = vec_ok && (col0 + 32 <= p.n);
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (out_f32) {
-          float *cp = static_cast<float *>(p.c) + b * p.stride_c + row * p.ldc + col0;
-          if (full_chunk) {
-            float4 *c4 = reinterpret_cast<float4 *>(cp);
-            if (accumulate) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 o = c4[j];
-                v[4 * j] += o.x; v[4 * j + 1] += o.y; v[4 * j + 2] += o.z; v[4 * j + 3] += o.w;
-              }
-            }
-            if (gelu) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = gelu_f32(v[j]);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) c4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
-              float x = v[j];
-              if (accumulate) x += cp[j];
-              if (gelu) x = gelu_f32(x);
-              cp[j] = x;
-            }
-          }
-        } else {
-          uint16_t *cp = static_cast<uint16_t *>(p.c) + b * p.stride_c + row * p.ldc + col0;
-          if (full_chunk) {
-            uint4 *c4 = reinterpret_cast<uint4 *>(cp);
-            if (accumulate) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 o = c4[j];
-                const uint16_t *h = reinterpret_cast<const uint16_t *>(&o);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[8 * j + e] += h2f(h[e]);
-              }
-            }
-            uint32_t packed[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float x0 = v[2 * j], x1 = v[2 * j + 1];
-              if (gelu) {
-                x0 = gelu_f32(__half2float(__float2half_rn(x0)));
-                x1 = gelu_f32(__half2float(__float2half_rn(x1)));
-              }
-              packed[j] = pack_h2(x0, x1);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              c4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
-              float x = v[j];
-              if (accumulate) x += h2f(cp[j]);
-              if (gelu) x = gelu_f32(__half2float(__float2half_rn(x)));
-              cp[j] = f2h(x);
-            }
-          }
-        }
+        store_chunk(p, b, row, col0, r, vec_ok, out_f32, accumulate, gelu);
       }
       tc_fence_before();
       mbar_arrive(&tmem_empty[buf]);
@@ -264,6 +269,177 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2).  A pair computes a
+// 256 x 256 tile: each CTA loads its own 128 rows of A and its own 128 columns
+// of B (non-multicast TMA, completion counted on the leader's barrier), the
+// leader issues M=256 N=256 MMAs that read both CTAs' shared memory, and each
+// CTA's TMEM receives its 128 accumulator rows.  Per CTA this halves the B
+// traffic through shared memory compared with the single-CTA kernel, which is
+// what keeps the tensor pipe fed (TMA fill + MMA operand reads stay under the
+// shared-memory bandwidth).
+constexpr int PB_N = 128;                      // B columns per CTA
+constexpr int P_A_BYTES = BM * BK * 2;         // 16 KB
+constexpr int P_B_BYTES = PB_N * BK * 2;       // 16 KB
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_STAGES = 6;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int PAIR_BM = 2 * BM;                // 256 rows per pair tile
+
+template <bool kBKMajor>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t *empty = full + P_STAGES;
+  uint64_t *tmem_full = empty + P_STAGES;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tmem_empty + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);   // leader: its own arrive_expect_tx; peers only add bytes
+      mbar_init(&empty[s], 1);  // one multicast commit per stage use
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 8);  // lane 0 of the 4 epilogue warps of both CTAs
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
+        int b, mt, nt;
+        tile_coords(p, t, b, mt, nt);  // mt counts 256-row pair tiles
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *a_s = smem + s * P_STAGE_BYTES;
+          uint8_t *b_s = a_s + P_A_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE_BYTES);
+          tma_load_3d_pair(a_s, &tmA, &full[s], kb * BK, mt * PAIR_BM + (int)rank * BM, b);
+          if (kBKMajor) {
+            tma_load_3d_pair(b_s, &tmB, &full[s], kb * BK, nt * BN + (int)rank * PB_N, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < PB_N / 64; ++j)
+              tma_load_3d_pair(b_s + j * 8192, &tmB, &full[s], nt * BN + (int)rank * PB_N + j * 64, kb * BK, b);
+          }
+        }
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_PRODUCER);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*f16*/ 0, false, !kBKMajor);
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs, ++local) {
+        const uint32_t buf = local & 1u, use = local >> 1;
+        if (!mbar_wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * P_STAGE_BYTES);
+          const uint32_t b_addr = a_addr + P_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = make_smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bdesc = kBKMajor ? make_smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B)
+                                            : make_smem_desc(b_addr + k * 2048, 8192, 1024, kSwizzle128B);
+            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair(&tmem_full[buf], 0x3);
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_MMA);
+        *abort_flag = 1;
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const bool out_f32 = (p.flags & IPUC_GEMM_OUT_F32) != 0;
+    const bool accumulate = (p.flags & IPUC_GEMM_ACCUMULATE) != 0;
+    const bool gelu = (p.flags & IPUC_GEMM_EPILOGUE_GELU) != 0;
+    const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0);
+    uint32_t local = 0;
+    for (int64_t t = pair; t < p.num_tiles; t += pairs, ++local) {
+      const uint32_t buf = local & 1u, use = local >> 1;
+      if (!mbar_wait_bounded(&tmem_full[buf], use & 1u, abort_flag)) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_EPILOGUE);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int b, mt, nt;
+      tile_coords(p, t, b, mt, nt);
+      const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + buf * BN + chunk * 32 + ((uint32_t)(quarter * 32) << 16), r);
+        tmem_wait_ld(r);
+        const int64_t col0 = (int64_t)nt * BN + chunk * 32;
+        if (!row_ok || col0 >= p.n) continue;
+        store_chunk(p, b, row, col0, r, vec_ok, out_f32, accumulate, gelu);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_leader(&tmem_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -293,13 +469,35 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
   p.m = m; p.n = n; p.k = k; p.batch = batch;
   p.ldc = ldc;
   p.stride_c = batch > 1 ? sc : 0;
-  p.tiles_m = (int32_t)((m + BM - 1) / BM);
   p.tiles_n = (int32_t)((n + BN - 1) / BN);
   p.k_blocks = (int32_t)((k + BK - 1) / BK);
-  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   p.flags = flags;
   p.err = device_error_word();
-  const int grid = (int)(p.num_tiles < sm_count() ? p.num_tiles : sm_count());
+  const int sms = sm_count();
+  // CTA pairs once there are at least two 128-row tiles of work per pair slot.
+  const bool use_pair = m > BM && sms >= 2;
+  if (use_pair) {
+    p.tiles_m = (int32_t)((m + PAIR_BM - 1) / PAIR_BM);
+    p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
+    const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    CUtensorMap tap, tbp;
+    st = make_map_3d(&tap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, batch, lda, batch > 1 ? sa : 0, BK, BM);
+    if (st != IPUC_OK) return st;
+    if (bt) st = make_map_3d(&tbp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, k, n, batch, ldb, batch > 1 ? sb : 0, BK, PB_N);
+    else st = make_map_3d(&tbp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, n, k, batch, ldb, batch > 1 ? sb : 0, 64, BK);
+    if (st != IPUC_OK) return st;
+    if (bt) {
+      IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+      gemm_f16_pair_kernel<true><<<(unsigned)(2 * pairs), 192, P_SMEM_BYTES, stream>>>(tap, tbp, p);
+    } else {
+      IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+      gemm_f16_pair_kernel<false><<<(unsigned)(2 * pairs), 192, P_SMEM_BYTES, stream>>>(tap, tbp, p);
+    }
+    return check_launch("gemm_f16_pair_kernel");
+  }
+  p.tiles_m = (int32_t)((m + BM - 1) / BM);
+  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
+  const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
   if (bt) {
     IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     gemm_f16_kernel<true><<<grid, 192, SMEM_BYTES, stream>>>(ta, tb, p);
