@@ -6,11 +6,13 @@
 // device/attention_stages_f16.S:803-849).
 //
 // One CTA owns 256 query rows of one stream as two 128-row tiles (Q0, Q1) and
-// streams 128-key K/V tiles through a 2-stage TMA ring.  Warp roles:
+// streams 128-key K/V tiles through 2-stage TMA rings (K stages are released
+// as soon as both tiles' QK^T products finish, V stages after PV).  Warp roles:
 //   warp 0      TMA loads (Q once; K_j, V_j per key tile)
 //   warp 1      MMA issue: S_t = Q_t K_j^T into TMEM, then O_t += P_t V_j with
 //               P_t read straight from TMEM (it aliases S_t as packed f16)
-//   warps 2-5   softmax for Q0; warps 6-9 softmax for Q1 (thread = query row)
+//   warps 2-17  softmax: 8 warps per Q tile, two per TMEM lane quarter, each
+//               thread owning 64 of its query row's 128 scores
 // The two tiles ping-pong so the tensor core computes one tile's products
 // while the other tile's softmax runs.  TMEM: S0 | S1 | O0 | O1 (4 x 128 cols).
 // The softmax keeps an fp32 running max and denominator per row; the O rescale
@@ -36,7 +38,7 @@ constexpr int DP = 128;       // padded head dim
 constexpr int TILE_BYTES = TQ * DP * 2;   // 32 KB (two 16 KB swizzled halves)
 constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
-constexpr int NUM_THREADS = 320;
+constexpr int NUM_THREADS = 576;  // 2 + 16 warps
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 struct AttnParams {
@@ -60,13 +62,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *q_full = bars + 0;
   uint64_t *k_full = bars + 1;   // [2]
   uint64_t *v_full = bars + 3;   // [2]
-  uint64_t *kv_empty = bars + 5; // [2]
+  uint64_t *k_empty = bars + 5;  // [2] K stage free (its QK^T products done)
   uint64_t *s_full = bars + 7;   // [2] per Q tile
   uint64_t *p_ready = bars + 9;  // [2] per Q tile
   uint64_t *o_final = bars + 11;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+  uint64_t *v_empty = bars + 12; // [2] V stage free (its PV products done)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
+  __shared__ float xmax[2][2][TQ], xsum[2][2][TQ];  // [tile][column half][row]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t stream = blockIdx.y;
   const int32_t q0 = blockIdx.x * (2 * TQ);
@@ -77,9 +81,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], 128);
+      mbar_init(&p_ready[i], 256);
     }
     mbar_init(o_final, 1);
     *abort_flag = 0;
@@ -107,13 +112,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_load_3d(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * TQ, (int32_t)stream);
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait_bounded(&kv_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
+        if (!mbar_wait_bounded(&k_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sK + st * TILE_BYTES + h * HALF_BYTES, &tmK, &k_full[st], h * 64, j * TK, (int32_t)stream);
+        if (!mbar_wait_bounded(&v_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
         mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
         for (int h = 0; h < 2; ++h)
           tma_load_3d(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, j * TK, (int32_t)stream);
@@ -143,6 +152,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (ok) {
         issue_s(0, 0);
         issue_s(1, 0);
+        mma_commit(&k_empty[0]);
       }
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
@@ -164,7 +174,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             issue_s(t, nst);
           }
         }
-        mma_commit(&kv_empty[st]);
+        mma_commit(&v_empty[st]);
+        if (j + 1 < n_tiles) mma_commit(&k_empty[(j + 1) & 1]);
       }
       if (ok) mma_commit(o_final);
       if (!ok) {
@@ -173,48 +184,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // Softmax warpgroups: t = 0 for warps 2-5, 1 for warps 6-9.
-    const int t = (warp - 2) >> 2;
+    // Softmax: 16 warps.  Q tile t = (warp-2)/8; within a tile, column half
+    // h = ((warp-2)%8)/4 of the 128-key S tile, TMEM lane quarter warp%4.  The
+    // two warps sharing a lane quarter (h = 0, 1) own the same 32 query rows
+    // and exchange their partial row maxima through shared memory behind a
+    // 64-thread named barrier, so each thread exponentiates 64 scores.
+    const int sw = warp - 2;
+    const int t = sw >> 3;
+    const int h = (sw >> 2) & 1;
     const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t bar_id = 1 + t * 4 + quarter;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_col = tmem + lane_off + t * 128;
-    const uint32_t o_col = tmem + lane_off + 256 + t * 128;
+    const uint32_t o_col = tmem + lane_off + 256 + t * 128 + h * 64;
     const float c = p.scale_log2;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      // Pass 1: row max over the valid keys of this tile (S stays in TMEM).
-      const int64_t rem_keys = p.sk - (int64_t)j * TK;
-      const int valid = rem_keys < TK ? (int)rem_keys : TK;
-      const bool full_tile = valid == TK;
+      const int64_t rem_keys = p.sk - (int64_t)j * TK - h * 64;
+      const int valid = rem_keys < 64 ? (rem_keys > 0 ? (int)rem_keys : 0) : 64;
+      // This warp's 64 scores stay in registers (P overwrites S columns of the
+      // partner's half only after the barrier below).
+      uint32_t a[32], b[32];
+      tmem_ld_32x32b_x32(s_col + h * 64, a);
+      tmem_ld_32x32b_x32(s_col + h * 64 + 32, b);
+      tmem_wait_ld(a);
+      tmem_regs_fence(b);
       float mx = -INFINITY;
-      if (full_tile) {
+      if (valid == 64) {
         float mx1 = -INFINITY;
 #pragma unroll
-        for (int ch = 0; ch < TK / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(s_col + ch * 32, r);
-          tmem_wait_ld(r);
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            mx = max3(mx, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-            mx1 = max3(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-          }
+        for (int i = 0; i < 32; i += 4) {
+          mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(a[i + 1]));
+          mx1 = max3(mx1, __uint_as_float(a[i + 2]), __uint_as_float(a[i + 3]));
+          mx = max3(mx, __uint_as_float(b[i]), __uint_as_float(b[i + 1]));
+          mx1 = max3(mx1, __uint_as_float(b[i + 2]), __uint_as_float(b[i + 3]));
         }
         mx = fmaxf(mx, mx1);
       } else {
 #pragma unroll
-        for (int ch = 0; ch < TK / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(s_col + ch * 32, r);
-          tmem_wait_ld(r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (ch * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+        for (int i = 0; i < 32; ++i) {
+          if (i >= valid) a[i] = __float_as_uint(-INFINITY);
+          if (i + 32 >= valid) b[i] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, fmaxf(__uint_as_float(a[i]), __uint_as_float(b[i])));
         }
       }
+      xmax[t][h][row] = mx;
+      named_barrier_sync(bar_id, 64);
+      mx = fmaxf(mx, xmax[t][h ^ 1][row]);
       const float m_new = fmaxf(m, mx);
       bool rescale = false;
       float alpha = 1.0f;
@@ -226,108 +246,80 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         m = m_new;
         l *= alpha;
       }
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_t is stable: PV_t(j-1) was issued before S_t(j), whose completion we observed.
-#pragma unroll
-        for (int ch = 0; ch < DP / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(o_col + ch * 32, r);
-          tmem_wait_ld(r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st_32x32b_x32(o_col + ch * 32, r);
-        }
-      }
+      // P = 2^(s*c - m*c) in packed f16 written to S columns [h*32, h*32+32):
+      // packed f32x2 arithmetic, one pair in four exponentiated on the FMA
+      // pipe (exp2_poly2) to unload the MUFU unit.  Masked keys hold -inf -> 0.
       const float mc = m * c;
-      float sum = 0.0f;
-      // Pass 2: P = 2^(s*c - m*c) as packed f16, written over the first 64
-      // columns of S.  Full tiles use packed f32x2 arithmetic and compute one
-      // pair in four on the FMA pipe (exp2_poly2) to unload the MUFU unit.
-      if (full_tile) {
-        const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
-        uint64_t sum2 = f2_pack(0.0f, 0.0f);
+      const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
+      uint64_t sum2 = f2_pack(0.0f, 0.0f);
+      uint32_t packed[32];
 #pragma unroll
-        for (int ch = 0; ch < TK / 64; ++ch) {
-          uint32_t a[32], b[32];
-          tmem_ld_32x32b_x32(s_col + ch * 64, a);
-          tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
-          tmem_wait_ld(a);
-          tmem_regs_fence(b);
-          uint32_t packed[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
-            const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
-            const uint64_t t = f2_fma(f2_pack(x0, x1), c2, nmc2);
-            uint64_t pp;
-            if ((i & 3) == 3) {
-              pp = exp2_poly2(t);
-            } else {
-              float t0, t1;
-              f2_unpack(t, t0, t1);
-              pp = f2_pack(ex2_approx(t0), ex2_approx(t1));
-            }
-            sum2 = f2_add(sum2, pp);
-            float p0, p1;
-            f2_unpack(pp, p0, p1);
-            __half2 h2 = __floats2half2_rn(p0, p1);
-            packed[i] = *reinterpret_cast<uint32_t *>(&h2);
-          }
-          tmem_st_32x32b_x32(s_col + ch * 32, packed);
+      for (int i = 0; i < 32; ++i) {
+        const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
+        const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
+        const uint64_t tt = f2_fma(f2_pack(x0, x1), c2, nmc2);
+        uint64_t pp;
+        if ((i & 3) == 3) {
+          pp = exp2_poly2(tt);
+        } else {
+          float t0, t1;
+          f2_unpack(tt, t0, t1);
+          pp = f2_pack(ex2_approx(t0), ex2_approx(t1));
         }
-        float s0, s1;
-        f2_unpack(sum2, s0, s1);
-        sum = s0 + s1;
-      } else {
+        sum2 = f2_add(sum2, pp);
+        float p0, p1;
+        f2_unpack(pp, p0, p1);
+        __half2 h2 = __floats2half2_rn(p0, p1);
+        packed[i] = *reinterpret_cast<uint32_t *>(&h2);
+      }
+      tmem_st_32x32b_x32(s_col + h * 32, packed);
+      float s0, s1;
+      f2_unpack(sum2, s0, s1);
+      l += s0 + s1;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_t is stable: PV_t(j-1) was issued before S_t(j), whose completion
+        // we observed.  Each warp rescales its 64 columns of O.
 #pragma unroll
-        for (int ch = 0; ch < TK / 64; ++ch) {
-          uint32_t a[32], b[32];
-          tmem_ld_32x32b_x32(s_col + ch * 64, a);
-          tmem_ld_32x32b_x32(s_col + ch * 64 + 32, b);
-          tmem_wait_ld(a);
-          tmem_regs_fence(b);
-          uint32_t packed[32];
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_col + ch * 32, o);
+          tmem_wait_ld(o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = ch * 64 + 2 * i;
-            const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
-            const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
-            const float p0 = col < valid ? ex2_approx(fmaf(x0, c, -mc)) : 0.0f;
-            const float p1 = col + 1 < valid ? ex2_approx(fmaf(x1, c, -mc)) : 0.0f;
-            sum += p0 + p1;
-            __half2 h2 = __floats2half2_rn(p0, p1);
-            packed[i] = *reinterpret_cast<uint32_t *>(&h2);
-          }
-          tmem_st_32x32b_x32(s_col + ch * 32, packed);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(o_col + ch * 32, o);
         }
       }
-      l += sum;
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_ready[t]);
     }
-    // Epilogue: O_t / l -> out.
+    // Epilogue: combine the two partial row sums, then O_t / l -> out for this
+    // warp's 64 columns.
+    xsum[t][h][row] = l;
+    named_barrier_sync(bar_id, 64);
+    l += xsum[t][h ^ 1][row];
     if (ok && mbar_wait_bounded(o_final, 0, abort_flag)) {
       tc_fence_after();
-      const int64_t row = (int64_t)q0 + t * TQ + quarter * 32 + lane;
+      const int64_t grow = (int64_t)q0 + t * TQ + row;
       const float inv = 1.0f / l;
-      const bool row_ok = row < p.sq;
-      const int64_t base = (stream * p.sq + row) * p.d;
+      const bool row_ok = grow < p.sq;
+      const int64_t base = (stream * p.sq + grow) * p.d;
 #pragma unroll
-      for (int ch = 0; ch < DP / 32; ++ch) {
+      for (int ch = 0; ch < 2; ++ch) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(o_col + ch * 32, r);
         tmem_wait_ld(r);
-        if (!row_ok || ch * 32 >= p.d) continue;
+        const int col0 = h * 64 + ch * 32;
+        if (!row_ok || col0 >= p.d) continue;
         if (p.out_f32) {
-          float *o = static_cast<float *>(p.out) + base + ch * 32;
-          for (int i = 0; i < 32 && ch * 32 + i < p.d; i += 4)
+          float *o = static_cast<float *>(p.out) + base + col0;
+          for (int i = 0; i < 32 && col0 + i < p.d; i += 4)
             *reinterpret_cast<float4 *>(o + i) =
                 make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
                             __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
         } else {
-          uint16_t *o = static_cast<uint16_t *>(p.out) + base + ch * 32;
-          for (int i = 0; i < 32 && ch * 32 + i < p.d; i += 8) {
+          uint16_t *o = static_cast<uint16_t *>(p.out) + base + col0;
+          for (int i = 0; i < 32 && col0 + i < p.d; i += 8) {
             uint4 v;
             v.x = pack_h2(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv);
             v.y = pack_h2(__uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
