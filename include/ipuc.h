@@ -235,6 +235,12 @@ ipuc_status ipuc_convert_order_f16(void *dst, ipuc_order to, const void *src, ip
 ipuc_status ipuc_split_heads_f16(void *out, const void *in, int64_t batch, int64_t rows,
                                  int64_t heads, int64_t channels, ipuc_stream stream);
 
+/* MergeHeads: [batch*heads, rows, channels] -> [batch, rows, heads*channels],
+ * the inverse of SplitHeads.  The reference graph has no such operator; it is
+ * what an attention block's output projection needs after per-head attention. */
+ipuc_status ipuc_merge_heads_f16(void *out, const void *in, int64_t batch, int64_t rows, int64_t heads,
+                                 int64_t channels, ipuc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

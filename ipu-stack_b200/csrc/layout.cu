@@ -29,11 +29,8 @@ struct Side {
   int32_t vec;         // 16-byte vector accesses allowed on the row-major side
 };
 
-// storage.rs:333-340 AMP-Output pair swizzle and its inverse (storage.rs:689-694).
-__device__ __forceinline__ int swz(int c) {
-  int lp = c >> 1, pp = (lp & 3) * 2 + (lp >> 2);
-  return pp * 2 + (c & 1);
-}
+// Inverse of the AMP-Output pair swizzle of storage.rs:333-340 (as in
+// amp_matrix_coordinates, storage.rs:689-694): physical column -> logical.
 __device__ __forceinline__ int unswz(int pc) {
   int pp = pc >> 1, lp = (pp & 1) * 4 + (pp >> 1);
   return lp * 2 + (pc & 1);
@@ -464,10 +461,47 @@ __global__ void split_heads_kernel(uint16_t *__restrict__ out, const uint16_t *_
   }
 }
 
+// MergeHeads [b*h, r, c] -> [b, r, h*c]: the inverse permutation.
+template <bool kVec>
+__global__ void merge_heads_kernel(uint16_t *__restrict__ out, const uint16_t *__restrict__ in, int64_t batch,
+                                   int64_t rows, int64_t heads, int64_t channels) {
+  const int64_t total = batch * heads * rows * channels;
+  const int64_t width = heads * channels;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * 8;
+  for (int64_t o = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; o < total; o += step) {
+    if (kVec) {
+      const int64_t wc = o % width, t = o / width, r = t % rows, b = t / rows;
+      const int64_t h = wc / channels, c = wc % channels;
+      *reinterpret_cast<uint4 *>(out + o) = *reinterpret_cast<const uint4 *>(in + ((b * heads + h) * rows + r) * channels + c);
+    } else {
+      for (int64_t e = o; e < o + 8 && e < total; ++e) {
+        const int64_t wc = e % width, t = e / width, r = t % rows, b = t / rows;
+        out[e] = in[((b * heads + wc / channels) * rows + r) * channels + wc % channels];
+      }
+    }
+  }
+}
+
 }  // namespace
 }  // namespace ipuc
 
 using namespace ipuc;
+
+extern "C" ipuc_status ipuc_merge_heads_f16(void *out, const void *in, int64_t batch, int64_t rows, int64_t heads,
+                                            int64_t channels, ipuc_stream stream) {
+  IPUC_CHECK_ARG(batch >= 0 && rows >= 0 && heads > 0 && channels > 0, "merge_heads: bad extents");
+  const int64_t total = batch * rows * heads * channels;
+  if (total == 0) return IPUC_OK;
+  const bool vec = channels % 8 == 0 && aligned(out, 16) && aligned(in, 16);
+  const int64_t chunks = (total + 7) / 8;
+  const int64_t want = (chunks + 255) / 256, cap = (int64_t)sm_count() * 16;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  if (vec)
+    merge_heads_kernel<true><<<grid, 256, 0, stream>>>((uint16_t *)out, (const uint16_t *)in, batch, rows, heads, channels);
+  else
+    merge_heads_kernel<false><<<grid, 256, 0, stream>>>((uint16_t *)out, (const uint16_t *)in, batch, rows, heads, channels);
+  return check_launch("merge_heads_kernel");
+}
 
 extern "C" ipuc_status ipuc_rearrange_f16(void *dst, const void *src, int64_t matrices, int64_t logical_rows,
                                           int64_t physical_rows, int32_t target_order, int64_t logical_columns,

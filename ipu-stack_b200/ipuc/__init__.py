@@ -55,6 +55,7 @@ SIGNATURES = {
     "ipuc_unpack_f16": (_i32, [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _vp]),
     "ipuc_convert_order_f16": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _vp]),
     "ipuc_split_heads_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "ipuc_merge_heads_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
 }
 
 
@@ -219,3 +220,7 @@ def convert_order_f16(dst, to, src, frm, matrices, rows, columns, row_block=64, 
 
 def split_heads_f16(out, inp, batch, rows, heads, channels, stream=None):
     call("ipuc_split_heads_f16", _ptr(out), _ptr(inp), batch, rows, heads, channels, _stream(stream))
+
+
+def merge_heads_f16(out, inp, batch, rows, heads, channels, stream=None):
+    call("ipuc_merge_heads_f16", _ptr(out), _ptr(inp), batch, rows, heads, channels, _stream(stream))

@@ -247,3 +247,48 @@ def unpack_f16(src_bits, source_order, matrices, R, Rp, C, Cp):
     if rc != 0:
         raise ValueError("unsupported unpack geometry")
     return dst
+
+
+# --------------------------------------------------------------------------
+# Whole-graph evaluation: evaluate_operations (diagnostic.rs:420-464)
+# --------------------------------------------------------------------------
+
+def _attention_batched(q, k, v, scale, threads):
+    lead = q.shape[:-2]
+    s = int(np.prod(lead)) if lead else 1
+    out = attention(q.reshape(s, *q.shape[-2:]), k.reshape(s, *k.shape[-2:]), v.reshape(s, *v.shape[-2:]),
+                    scale=scale, threads=threads)
+    return out.reshape(*lead, q.shape[-2], v.shape[-1])
+
+
+def evaluate(graph, inputs: dict, threads: int = 8) -> dict:
+    """Evaluate a recorded ComputeGraph (ipuc.graph.ComputeGraph) on f32 host
+    values.  `inputs` maps input value ids to arrays; every input is first
+    quantised to f16 (prepare_inputs, diagnostic.rs:324-341) and every op
+    result is quantised to f16 (diagnostic.rs:454-460).  Returns a dict of
+    value id -> f32 array."""
+    vals = {v: quantize_f16(np.asarray(a, dtype=np.float32)) for v, a in inputs.items()}
+    for op in graph.operations:
+        ins = [vals[i] for i in op.inputs]
+        if op.kind == "gemm":
+            r = gemm(ins[0], ins[1], op.options["transpose_left"], op.options["transpose_right"])
+        elif op.kind == "gelu":
+            r = gelu(ins[0])
+        elif op.kind == "add":
+            r = (ins[0] + ins[1]).astype(np.float32)
+        elif op.kind == "split_heads":
+            b, rows, w = ins[0].shape
+            h = op.options["heads"]
+            r = ins[0].reshape(b, rows, h, w // h).transpose(0, 2, 1, 3).reshape(b * h, rows, w // h)
+        elif op.kind == "merge_heads":
+            bh, rows, c = ins[0].shape
+            h = op.options["heads"]
+            r = ins[0].reshape(bh // h, h, rows, c).transpose(0, 2, 1, 3).reshape(bh // h, rows, h * c)
+        elif op.kind == "flash_attention":
+            if op.options.get("causal"):
+                raise NotImplementedError("causal attention")
+            r = _attention_batched(ins[0], ins[1], ins[2], op.options.get("scale"), threads)
+        else:
+            raise ValueError(op.kind)
+        vals[op.result] = quantize_f16(np.ascontiguousarray(r, dtype=np.float32))
+    return vals

@@ -1,0 +1,100 @@
+"""ComputeGraph -> per-GPU lowering -> session, checked end to end against the
+oracle's restatement of the host evaluator (diagnostic.rs:411-847), with the
+FP16 tolerance max|err| <= 2e-2*max|ref|, rel-L2 <= 5e-3."""
+import numpy as np
+import pytest
+
+import ipuc
+import oracle
+from conftest import f16_close, seeded_normal
+from ipuc.graph import ComputeGraph, Session
+
+pytestmark = pytest.mark.gpu
+
+
+def run_graph(g, inputs):
+    s = Session(g)
+    for v, a in inputs.items():
+        s.write(v, a)
+    s.run()
+    return s
+
+
+def test_mlp_chain_fuses_gelu():
+    """mlp-smoke structure (main.rs:1996-2033): GEMM-GELU-GEMM-GELU, 64 wide."""
+    g = ComputeGraph()
+    x = g.host_input("input", [16, 64])
+    w0 = g.parameter("w0", [64, 64])
+    w1 = g.parameter("w1", [64, 64])
+    y = g.gelu(g.gemm(g.gelu(g.gemm(x, w0)), w1))
+    g.set_outputs([y])
+    inputs = {x: seeded_normal(1, (16, 64), 0.5), w0: seeded_normal(2, (64, 64), 0.125),
+              w1: seeded_normal(3, (64, 64), 0.125)}
+    s = run_graph(g, inputs)
+    assert s.plan.count("gemm_f16+gelu") == 2
+    ref = oracle.evaluate(g, inputs)[y]
+    ok, msg = f16_close(s.read(y).astype(np.float32), ref)
+    assert ok, msg
+
+
+def build_block(B, S, d, H, ff):
+    g = ComputeGraph()
+    x = g.host_input("x", [B, S, d])
+    ws = {n: g.parameter(n, shp) for n, shp in [("wq", [d, d]), ("wk", [d, d]), ("wv", [d, d]), ("wo", [d, d]),
+                                                ("w1", [d, ff]), ("w2", [ff, d])]}
+    q = g.split_heads(g.gemm(x, ws["wq"]), H)
+    k = g.split_heads(g.gemm(x, ws["wk"]), H)
+    v = g.split_heads(g.gemm(x, ws["wv"]), H)
+    a = g.merge_heads(g.flash_attention(q, k, v), H)
+    h = g.add(g.gemm(a, ws["wo"]), x)                  # residual add fused into the GEMM
+    out = g.add(g.gemm(g.gelu(g.gemm(h, ws["w1"])), ws["w2"]), h)
+    g.set_outputs([out])
+    return g, x, ws, out
+
+
+def test_transformer_block_small():
+    """Config-5 structure at small size: QKV projections, per-head attention,
+    output projection + residual, MLP with GELU + residual."""
+    B, S, d, H, ff = 2, 256, 256, 4, 1024
+    g, x, ws, out = build_block(B, S, d, H, ff)
+    rng = np.random.default_rng(7)
+    inputs = {x: rng.standard_normal((B, S, d)).astype(np.float32)}
+    for n, v in ws.items():
+        inputs[v] = (rng.standard_normal(g.value_shape(v)) * 0.02).astype(np.float32)
+    s = run_graph(g, inputs)
+    plan = s.plan
+    assert plan.count("gemm_f16+add") == 2 and plan.count("gemm_f16+gelu") == 1
+    assert "flash_attention_f16" in plan and "merge_heads_f16" in plan
+    ref = oracle.evaluate(g, inputs)[out]
+    ok, msg = f16_close(s.read(out).astype(np.float32), ref)
+    assert ok, msg
+    prof = s.profile()
+    assert len(prof["steps"]) == plan.count("\n") and prof["total_ms"] > 0
+    assert any("tflops" in st for st in prof["steps"])
+
+
+def test_bias_broadcast_add_and_unfused_gemm():
+    g = ComputeGraph()
+    x = g.host_input("x", [64, 128])
+    w = g.parameter("w", [128, 256])
+    b = g.parameter("b", [256])
+    y = g.gemm(x, w)
+    z = g.add(y, b)          # bias: broadcast add, not fused
+    r = g.gelu(y)            # second consumer keeps the GEMM unfused
+    g.set_outputs([z, r])
+    inputs = {x: seeded_normal(4, (64, 128)), w: seeded_normal(5, (128, 256), 0.1), b: seeded_normal(6, (256,))}
+    s = run_graph(g, inputs)
+    assert "gemm_f16 " in s.plan and "add_f16" in s.plan and "gelu_f16" in s.plan
+    ref = oracle.evaluate(g, inputs)
+    for v in (z, r):
+        ok, msg = f16_close(s.read(v).astype(np.float32), ref[v])
+        assert ok, msg
+
+
+def test_unsupported_features_fail_loudly():
+    g = ComputeGraph()
+    q = g.host_input("q", [2, 64, 64])
+    g.flash_attention_with_options(q, q, q, causal=True)
+    with pytest.raises(ipuc.IpucError) as e:
+        Session(g)
+    assert e.value.status == ipuc.ERR_UNSUPPORTED

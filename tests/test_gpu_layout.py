@@ -73,3 +73,13 @@ def test_split_heads_bit_exact(b, r, h, c):
     out = empty_u16(x.size)
     ipuc.split_heads_f16(out, dev_u16(x), b, r, h, c)
     assert np.array_equal(host_u16(out), want.ravel())
+
+
+@pytest.mark.parametrize("b,r,h,c", [(2, 33, 4, 16), (1, 7, 3, 5)])
+def test_merge_heads_inverts_split_heads(b, r, h, c):
+    x = bits(b * r * h + c, b * r * h * c).reshape(b, r, h * c)
+    split = empty_u16(x.size)
+    ipuc.split_heads_f16(split, dev_u16(x), b, r, h, c)
+    back = empty_u16(x.size)
+    ipuc.merge_heads_f16(back, split, b, r, h, c)
+    assert np.array_equal(host_u16(back), x.ravel())
