@@ -361,6 +361,48 @@ def measure_components(ipuc, torch, stream, hbm_gbs):
         out["gemm_f32_4096"] = {"ms": round(ms, 4), "tflops": round(2 * m * n_ * k / (ms * 1e-3) / 1e12, 1)}
     except ipuc.IpucError as e:
         out["gemm_f32_4096"] = {"unavailable": str(e)}
+    del a32, b32, c32, ws
+    torch.cuda.empty_cache()
+    out["transformer_block"] = transformer_block(ipuc, torch, stream)
+    return out
+
+
+def transformer_block(ipuc, torch, stream):
+    """Config 5 lowered end to end through the ComputeGraph session on one GPU:
+    batch 4 x seq 2048 (8192 tokens), d=4096, 32 heads of 128, MLP 4096->16384
+    ->4096 with GELU, two residual adds; weights N(0, 0.02), f16."""
+    import numpy as np
+    from ipuc.graph import ComputeGraph, Session
+    B, S, d, H, ff = 4, 2048, 4096, 32, 16384
+    g = ComputeGraph()
+    x = g.host_input("x", [B, S, d])
+    w = {n: g.parameter(n, shp) for n, shp in [("wq", [d, d]), ("wk", [d, d]), ("wv", [d, d]), ("wo", [d, d]),
+                                               ("w1", [d, ff]), ("w2", [ff, d])]}
+    q = g.split_heads(g.gemm(x, w["wq"]), H)
+    k = g.split_heads(g.gemm(x, w["wk"]), H)
+    v = g.split_heads(g.gemm(x, w["wv"]), H)
+    a = g.merge_heads(g.flash_attention(q, k, v), H)
+    h = g.add(g.gemm(a, w["wo"]), x)
+    y = g.add(g.gemm(g.gelu(g.gemm(h, w["w1"])), w["w2"]), h)
+    g.set_outputs([y])
+    sess = Session(g)
+    rng = np.random.default_rng(5)
+    sess.write(x, rng.standard_normal((B, S, d), dtype=np.float32))
+    for name, val in w.items():
+        sess.write(val, rng.standard_normal(g.value_shape(val), dtype=np.float32) * np.float32(0.02))
+    flop = 2.0 * B * S * d * d * 4 + 4.0 * B * H * S * S * (d // H) + 2 * 2.0 * B * S * d * ff
+    for _ in range(2):
+        sess.run(stream)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record(stream)
+    for _ in range(5):
+        sess.run(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 5
+    out = {"ms": round(ms, 4), "tflops": round(flop / (ms * 1e-3) / 1e12, 1), "flop": flop,
+           "steps": sess.plan.count("\n")}
+    sess.close()
     return out
 
 
