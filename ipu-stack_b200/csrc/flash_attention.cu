@@ -50,6 +50,12 @@ struct AttnParams {
   uint32_t *err;
 };
 
+// kPair: the kernel runs as 2-CTA clusters issuing cta_group::2 MMAs
+// (M = 256 query rows over the pair).  Each CTA then loads only its half of
+// every K tile (64 keys) and of every V tile (64 head-dim columns), halving
+// per-CTA shared-memory fill and B-operand reads; the leader (rank 0) issues
+// all MMAs and both CTAs' softmax warps run as in the single-CTA kernel.
+template <bool kPair>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -73,7 +79,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ float xmax[2][2][TQ], xsum[2][2][TQ];  // [tile][column half][row]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t stream = blockIdx.y;
-  const int32_t q0 = blockIdx.x * (2 * TQ);
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int32_t q0 = kPair ? (int32_t)(blockIdx.x >> 1) * (4 * TQ) + (int32_t)rank * (2 * TQ)
+                           : (int32_t)blockIdx.x * (2 * TQ);
+  constexpr int K_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA K tile (64 or 128 keys)
+  constexpr int K_HALF = K_BYTES / 2;                             // one 64-column head-dim half
+  constexpr int V_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA V tile (64 or 128 D columns)
+  constexpr int TX_MULT = kPair ? 2 : 1;                          // leader counts both CTAs' bytes
   const int n_tiles = p.key_tiles;
 
   if (threadIdx.x == 0) {
@@ -84,7 +97,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], 256);
+      mbar_init(&p_ready[i], kPair ? 16 : 8);  // lane 0 of each softmax warp of the tile
     }
     mbar_init(o_final, 1);
     *abort_flag = 0;
@@ -94,11 +107,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmV);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
+    if (kPair) {
+      tmem_alloc_pair(tmem_slot, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (kPair) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // TMEM columns: S_t at t*128, O_t at 256 + t*128.
@@ -106,26 +125,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+      auto load = [&](void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x, int32_t y) {
+        if (kPair) tma_load_3d_pair(dst, map, bar, x, y, (int32_t)stream);
+        else tma_load_3d(dst, map, bar, x, y, (int32_t)stream);
+      };
+      if (leader) mbar_arrive_expect_tx(q_full, TX_MULT * 2 * TILE_BYTES);
       for (int t = 0; t < 2; ++t)
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * TQ, (int32_t)stream);
+        for (int h = 0; h < 2; ++h) load(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * TQ);
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
         if (!mbar_wait_bounded(&k_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        if (leader) mbar_arrive_expect_tx(&k_full[st], TX_MULT * K_BYTES);
         for (int h = 0; h < 2; ++h)
-          tma_load_3d(sK + st * TILE_BYTES + h * HALF_BYTES, &tmK, &k_full[st], h * 64, j * TK, (int32_t)stream);
+          load(sK + st * TILE_BYTES + h * K_HALF, &tmK, &k_full[st], h * 64, j * TK + (int32_t)rank * (TK / 2));
         if (!mbar_wait_bounded(&v_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, j * TK, (int32_t)stream);
+        if (leader) mbar_arrive_expect_tx(&v_full[st], TX_MULT * V_BYTES);
+        if (kPair) {
+          load(sV + st * TILE_BYTES, &tmV, &v_full[st], (int32_t)rank * 64, j * TK);
+        } else {
+          for (int h = 0; h < 2; ++h) load(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, j * TK);
+        }
       }
       if (!ok) {
         record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_PRODUCER);
@@ -133,26 +158,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc(TQ, TK, 0, false, false);  // K-major Q and K
-      constexpr uint32_t idesc_o = make_idesc(TQ, DP, 0, false, true);   // V is MN-major (D contiguous)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc(kPair ? 2 * TQ : TQ, TK, 0, false, false);  // K-major Q and K
+      constexpr uint32_t idesc_o = make_idesc(kPair ? 2 * TQ : TQ, DP, 0, false, true);   // V MN-major (D contiguous)
+      auto commit = [&](uint64_t *bar) {
+        if (kPair) mma_commit_pair(bar, 0x3);
+        else mma_commit(bar);
+      };
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       auto issue_s = [&](int t, int stage) {
         const uint32_t qa = q_addr + t * TILE_BYTES, ka = k_addr + stage * TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < DP / 16; ++k) {
-          const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-          mma_f16_ss(tmem + t * 128, make_smem_desc(qa + off, 16, 1024, kSwizzle128B),
-                     make_smem_desc(ka + off, 16, 1024, kSwizzle128B), idesc_s, k > 0 ? 1u : 0u);
+          const uint64_t adesc = make_smem_desc(qa + (k >> 2) * HALF_BYTES + (k & 3) * 32, 16, 1024, kSwizzle128B);
+          const uint64_t bdesc = make_smem_desc(ka + (k >> 2) * K_HALF + (k & 3) * 32, 16, 1024, kSwizzle128B);
+          if (kPair) mma_f16_ss_pair(tmem + t * 128, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+          else mma_f16_ss(tmem + t * 128, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[t]);
+        commit(&s_full[t]);
       };
       if (ok) ok = mbar_wait_bounded(&k_full[0], 0, abort_flag);
       if (ok) {
         issue_s(0, 0);
         issue_s(1, 0);
-        mma_commit(&k_empty[0]);
+        commit(&k_empty[0]);
       }
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
@@ -164,9 +194,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < TK / 16; ++k) {
             // A = P_t (f16, 8 TMEM columns per 16 keys); B = V rows [16k, 16k+16)
-            mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8,
-                       make_smem_desc(va + k * 2048, HALF_BYTES, 1024, kSwizzle128B), idesc_o,
-                       (j > 0 || k > 0) ? 1u : 0u);
+            const uint64_t bdesc = make_smem_desc(va + k * 2048, HALF_BYTES, 1024, kSwizzle128B);
+            if (kPair) mma_f16_ts_pair(tmem + 256 + t * 128, tmem + t * 128 + k * 8, bdesc, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+            else mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8, bdesc, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
           }
           if (j + 1 < n_tiles) {
             const int nst = (j + 1) & 1;
@@ -174,10 +204,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             issue_s(t, nst);
           }
         }
-        mma_commit(&v_empty[st]);
-        if (j + 1 < n_tiles) mma_commit(&k_empty[(j + 1) & 1]);
+        commit(&v_empty[st]);
+        if (j + 1 < n_tiles) commit(&k_empty[(j + 1) & 1]);
       }
-      if (ok) mma_commit(o_final);
+      if (ok) commit(o_final);
       if (!ok) {
         record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_MMA);
         *abort_flag = 1;
@@ -291,7 +321,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_ready[t]);
+      __syncwarp();
+      if (lane == 0) {
+        if (kPair) mbar_arrive_leader(&p_ready[t]);
+        else mbar_arrive(&p_ready[t]);
+      }
     }
     // Epilogue: combine the two partial row sums, then O_t / l -> out for this
     // warp's 64 columns.
@@ -339,9 +373,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (kPair) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if (kPair) tmem_dealloc_pair(tmem, 512);
+    else tmem_dealloc(tmem, 512);
   }
 }
 
@@ -364,12 +400,14 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
                    "flash_attention: pointers must be 16-byte aligned");
   IPUC_CHECK_ARG(matrices < 65536 && query_rows < (1ll << 31) && key_rows < (1ll << 31),
                  "flash_attention: extent too large");
+  // CTA pairs when every pair gets a full 512-row query block.
+  const bool pair = query_rows >= 4 * TQ;
   CUtensorMap tq, tk, tv;
   ipuc_status st = make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q, head_dim, query_rows, matrices, head_dim,
                                query_rows * head_dim, 64, TQ);
   if (st != IPUC_OK) return st;
   st = make_map_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, k, head_dim, key_rows, matrices, head_dim,
-                   key_rows * head_dim, 64, TK);
+                   key_rows * head_dim, 64, pair ? TK / 2 : TK);
   if (st != IPUC_OK) return st;
   st = make_map_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v, head_dim, key_rows, matrices, head_dim,
                    key_rows * head_dim, 64, TK);
@@ -385,8 +423,25 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
   p.out_f32 = out_precision == IPUC_F32;
   p.key_tiles = (int32_t)((key_rows + TK - 1) / TK);
   p.err = device_error_word();
-  IPUC_CUDA(cudaFuncSetAttribute(flash_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  dim3 grid((unsigned)((query_rows + 2 * TQ - 1) / (2 * TQ)), (unsigned)matrices);
-  flash_attention_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  if (pair) {
+    IPUC_CUDA(cudaFuncSetAttribute(flash_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * ((query_rows + 4 * TQ - 1) / (4 * TQ))), (unsigned)matrices);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    IPUC_CUDA(cudaLaunchKernelEx(&cfg, flash_attention_kernel<true>, tq, tk, tv, p));
+  } else {
+    IPUC_CUDA(cudaFuncSetAttribute(flash_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    dim3 grid((unsigned)((query_rows + 2 * TQ - 1) / (2 * TQ)), (unsigned)matrices);
+    flash_attention_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  }
   return check_launch("flash_attention_kernel");
 }
