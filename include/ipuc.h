@@ -70,6 +70,12 @@ const char *ipuc_last_error_string(void);
  * "fails" only by host-side timeout (device/static_runtime.S:487-488). */
 ipuc_status ipuc_device_status(ipuc_stream stream);
 
+/* Exercises the bounded-wait failure path on the device: a kernel waits on an
+ * mbarrier that is never signalled, gives up after limit_ns (<= 10 s), sets
+ * the device error word and exits.  A following ipuc_device_status() returns
+ * IPUC_ERR_DEVICE_TIMEOUT.  Nothing faults or traps. */
+ipuc_status ipuc_selftest_bounded_wait(uint64_t limit_ns, ipuc_stream stream);
+
 /* FillZero: device/static_runtime.S:269-316, ABI kernel.rs:1224-1229.
  * bytes % 8 == 0 (validate_kernel_run, kernel.rs:1425-1434). */
 ipuc_status ipuc_fill_zero(void *out, uint64_t bytes, ipuc_stream stream);

@@ -4,6 +4,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace ipuc {
 
@@ -95,4 +96,28 @@ extern "C" ipuc_status ipuc_fill_zero(void *out, uint64_t bytes, ipuc_stream str
   IPUC_CHECK_ARG(out != nullptr, "fill_zero: null output");
   IPUC_CUDA(cudaMemsetAsync(out, 0, bytes, stream));
   return IPUC_OK;
+}
+
+// Self-test of the bounded-wait failure path: one thread waits on an mbarrier
+// that nothing ever arrives on, gives up after `limit_ns`, records the device
+// error word and returns — the same path every tensor-core kernel takes when a
+// pipeline partner never signals.  No trap, no fault; the context stays usable.
+namespace {
+__global__ void bounded_wait_selftest_kernel(uint32_t *err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    ipuc::sm100::mbar_init(&bar, 1);
+    ipuc::sm100::fence_barrier_init();
+    if (!ipuc::sm100::mbar_wait_bounded(&bar, 0, nullptr, limit_ns))
+      ipuc::record_device_error(err, ipuc::ERR_KERNEL_SELFTEST | ipuc::ERR_SITE_PRODUCER);
+  }
+}
+}  // namespace
+
+extern "C" ipuc_status ipuc_selftest_bounded_wait(uint64_t limit_ns, ipuc_stream stream) {
+  IPUC_CHECK_ARG(limit_ns > 0 && limit_ns <= 10000000000ull, "selftest: limit must be in (0, 10 s]");
+  uint32_t *word = device_error_word();
+  if (!word) return fail(IPUC_ERR_CUDA, "device error word unavailable");
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(word, limit_ns);
+  return check_launch("bounded_wait_selftest_kernel");
 }

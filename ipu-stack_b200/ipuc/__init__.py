@@ -38,6 +38,7 @@ SIGNATURES = {
     "ipuc_last_error_string": (ctypes.c_char_p, []),
     "ipuc_device_status": (_i32, [_vp]),
     "ipuc_fill_zero": (_i32, [_vp, _u64, _vp]),
+    "ipuc_selftest_bounded_wait": (_i32, [_u64, _vp]),
     "ipuc_gemm_f16": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _u32, _vp]),
     "ipuc_gemm_f16_batched": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                      _u32, _vp]),
