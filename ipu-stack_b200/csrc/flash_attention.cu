@@ -166,46 +166,64 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         else mma_commit(bar);
       };
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      // Descriptors are built once; each k-step adds a compile-time offset (in
+      // 16-byte units) so the single issuing thread spends about one integer
+      // add per MMA and keeps the tensor pipe fed.
+      const uint64_t q_desc = make_smem_desc(smem_u32(sQ), 16, 1024, kSwizzle128B);
+      const uint64_t k_desc = make_smem_desc(smem_u32(sK), 16, 1024, kSwizzle128B);
+      const uint64_t v_desc = make_smem_desc(smem_u32(sV), HALF_BYTES, 1024, kSwizzle128B);
       auto issue_s = [&](int t, int stage) {
-        const uint32_t qa = q_addr + t * TILE_BYTES, ka = k_addr + stage * TILE_BYTES;
+        const uint64_t qd = q_desc + (uint64_t)(t * (TILE_BYTES >> 4));
+        const uint64_t kd = k_desc + (uint64_t)(stage * (TILE_BYTES >> 4));
+        const uint32_t d = tmem + t * 128;
 #pragma unroll
         for (int k = 0; k < DP / 16; ++k) {
-          const uint64_t adesc = make_smem_desc(qa + (k >> 2) * HALF_BYTES + (k & 3) * 32, 16, 1024, kSwizzle128B);
-          const uint64_t bdesc = make_smem_desc(ka + (k >> 2) * K_HALF + (k & 3) * 32, 16, 1024, kSwizzle128B);
-          if (kPair) mma_f16_ss_pair(tmem + t * 128, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
-          else mma_f16_ss(tmem + t * 128, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+          const uint64_t adesc = qd + (uint64_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
+          const uint64_t bdesc = kd + (uint64_t)(((k >> 2) * K_HALF + (k & 3) * 32) >> 4);
+          if (kPair) mma_f16_ss_pair(d, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+          else mma_f16_ss(d, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
         }
         commit(&s_full[t]);
       };
+      // Issue order per key tile j (stage st = j & 1):
+      //   [P_0(j)] PV_0(j), (release K stage of tile j after its last use)
+      //            S_0(j+1)
+      //   [P_1(j)] PV_1(j), release V stage st, [V(j+1) landed], S_1(j+1)
+      // The bookkeeping between S_1(j+1) and PV_0(j+1) -- when the tensor
+      // pipe may run dry -- is one commit and the P_0 wait.
       if (ok) ok = mbar_wait_bounded(&k_full[0], 0, abort_flag);
       if (ok) {
         issue_s(0, 0);
         issue_s(1, 0);
-        commit(&k_empty[0]);
       }
+      if (ok) ok = mbar_wait_bounded(&v_full[0], 0, abort_flag);
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait_bounded(&v_full[st], (j >> 1) & 1, abort_flag)) { ok = false; break; }
+        const bool more = j + 1 < n_tiles;
+        const uint64_t vd = v_desc + (uint64_t)(st * (TILE_BYTES >> 4));
         for (int t = 0; t < 2 && ok; ++t) {
           if (!mbar_wait_bounded(&p_ready[t], j & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t va = v_addr + st * TILE_BYTES;
+          const uint32_t d = tmem + 256 + t * 128, a = tmem + t * 128;
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
           for (int k = 0; k < TK / 16; ++k) {
             // A = P_t (f16, 8 TMEM columns per 16 keys); B = V rows [16k, 16k+16)
-            const uint64_t bdesc = make_smem_desc(va + k * 2048, HALF_BYTES, 1024, kSwizzle128B);
-            if (kPair) mma_f16_ts_pair(tmem + 256 + t * 128, tmem + t * 128 + k * 8, bdesc, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-            else mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + k * 8, bdesc, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+            const uint64_t bdesc = vd + (uint64_t)((k * 2048) >> 4);
+            if (kPair) mma_f16_ts_pair(d, a + k * 8, bdesc, idesc_o, k > 0 ? 1u : acc0);
+            else mma_f16_ts(d, a + k * 8, bdesc, idesc_o, k > 0 ? 1u : acc0);
           }
-          if (j + 1 < n_tiles) {
-            const int nst = (j + 1) & 1;
-            if (t == 0 && !mbar_wait_bounded(&k_full[nst], ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-            issue_s(t, nst);
+          if (t == 0) {
+            // K stage st was last read by S_1(j), complete before P_1(j) could
+            // have been produced; release it now that PV_0(j) is queued.
+            commit(&k_empty[st]);
+            if (more && !mbar_wait_bounded(&k_full[st ^ 1], ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+          } else {
+            commit(&v_empty[st]);
+            if (more && !mbar_wait_bounded(&v_full[st ^ 1], ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
           }
+          if (more) issue_s(t, st ^ 1);
         }
-        commit(&v_empty[st]);
-        if (j + 1 < n_tiles) commit(&k_empty[(j + 1) & 1]);
       }
       if (ok) commit(o_final);
       if (!ok) {

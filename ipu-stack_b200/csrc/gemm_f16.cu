@@ -197,6 +197,8 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc = make_idesc(BM, BN, /*f16*/ 0, false, !kBKMajor);
       uint32_t it = 0, local = 0;
       bool ok = true;
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      const uint64_t b_desc0 = make_smem_desc(smem_u32(smem) + A_BYTES, kBKMajor ? 16 : 8192, 1024, kSwizzle128B);
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
         const uint32_t buf = local & 1u, use = local >> 1;
         if (!mbar_wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
@@ -213,13 +215,14 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_BYTES;
+          // Stage descriptors = base + stage offset; k-steps add compile-time
+          // offsets (16-byte units), keeping the issuing thread ahead of the pipe.
+          const uint64_t ad = a_desc0 + (uint64_t)(s * (STAGE_BYTES >> 4));
+          const uint64_t bd = b_desc0 + (uint64_t)(s * (STAGE_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = make_smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bdesc = kBKMajor ? make_smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B)
-                                            : make_smem_desc(b_addr + k * 2048, 8192, 1024, kSwizzle128B);
+            const uint64_t adesc = ad + (uint64_t)((k * 32) >> 4);
+            const uint64_t bdesc = bd + (uint64_t)((kBKMajor ? k * 32 : k * 2048) >> 4);
             mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           mma_commit(&empty[s]);
@@ -367,6 +370,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*f16*/ 0, false, !kBKMajor);
       uint32_t it = 0, local = 0;
       bool ok = true;
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      const uint64_t b_desc0 = make_smem_desc(smem_u32(smem) + P_A_BYTES, kBKMajor ? 16 : 8192, 1024, kSwizzle128B);
       for (int64_t t = pair; t < p.num_tiles && ok; t += pairs, ++local) {
         const uint32_t buf = local & 1u, use = local >> 1;
         if (!mbar_wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
@@ -383,13 +388,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + s * P_STAGE_BYTES);
-          const uint32_t b_addr = a_addr + P_A_BYTES;
+          // Stage descriptors = base + stage offset; k-steps add compile-time
+          // offsets (16-byte units), keeping the issuing thread ahead of the pipe.
+          const uint64_t ad = a_desc0 + (uint64_t)(s * (P_STAGE_BYTES >> 4));
+          const uint64_t bd = b_desc0 + (uint64_t)(s * (P_STAGE_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = make_smem_desc(a_addr + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bdesc = kBKMajor ? make_smem_desc(b_addr + k * 32, 16, 1024, kSwizzle128B)
-                                            : make_smem_desc(b_addr + k * 2048, 8192, 1024, kSwizzle128B);
+            const uint64_t adesc = ad + (uint64_t)((k * 32) >> 4);
+            const uint64_t bdesc = bd + (uint64_t)((kBKMajor ? k * 32 : k * 2048) >> 4);
             mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           mma_commit_pair(&empty[s], 0x3);

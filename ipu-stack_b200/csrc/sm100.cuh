@@ -47,19 +47,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: spins until the phase with `parity` completes, or until
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// parked (it issues nothing) until the phase completes or about `hint_ns`
+// pass, so waiting role warps leave the issue slots of their SM sub-partition
+// to the working warps.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: parks until the phase with `parity` completes, or until
 // `limit_ns` of global time have passed (returns false), or until *abort is
 // set by another role of the same CTA (returns false).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort,
                                                   uint64_t limit_ns = 4000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t spin = 1;; ++spin) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 0) {
-      if (abort && *abort) return false;
-      if (global_timer_ns() - t0 > limit_ns) return false;
-    }
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, 100000u)) return true;
+    if (abort && *abort) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 
