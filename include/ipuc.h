@@ -247,6 +247,122 @@ ipuc_status ipuc_split_heads_f16(void *out, const void *in, int64_t batch, int64
 ipuc_status ipuc_merge_heads_f16(void *out, const void *in, int64_t batch, int64_t rows, int64_t heads,
                                  int64_t channels, ipuc_stream stream);
 
+/* ---- Spec-driven dispatch ---------------------------------------------------
+ * The reference selects a tile kernel from a TileKernelSpec (operator.rs:57-96),
+ * derives its ABI with tile_kernel_abi (kernel.rs:1215-1382: symbol,
+ * availability, pointer inputs, named u32 scalars) and checks each run with
+ * validate_kernel_run (kernel.rs:1384-1435) before the call is materialised
+ * (KernelBuildPlan::call, kernel.rs:713-806).  ipuc_query_abi and ipuc_launch
+ * are that pair for one GPU shard: the spec and the scalar vector a reference
+ * call site builds are passed unchanged, operands are device tensors, and the
+ * call is routed to the typed entry point above. */
+
+/* TileKernelSpec discriminant (operator.rs:57-96). */
+typedef enum {
+  IPUC_KERNEL_FILL_ZERO = 0,
+  IPUC_KERNEL_GEMM = 1,
+  IPUC_KERNEL_GELU = 2,
+  IPUC_KERNEL_REDUCTION_SUM = 3,
+  IPUC_KERNEL_ADD = 4,
+  IPUC_KERNEL_FLASH_ATTENTION = 5,
+  IPUC_KERNEL_ATTENTION_SOFTMAX = 6,
+  IPUC_KERNEL_ATTENTION_MERGE = 7,
+  IPUC_KERNEL_CAST = 8,
+  IPUC_KERNEL_REARRANGE = 9
+} ipuc_kernel_kind;
+
+/* Layout {order} with the BlockMajorOrder block geometry (layout.rs:7-45). */
+typedef struct {
+  ipuc_order order;
+  uint32_t row_block;    /* BLOCK_MAJOR[_TRANSPOSED]; 0 elsewhere */
+  uint32_t column_block;
+} ipuc_layout;
+
+/* One TileKernelSpec.  Only the member of `kind` is read. */
+typedef struct {
+  ipuc_kernel_kind kind;
+  struct {                     /* Gemm (operator.rs:59-66) */
+    ipuc_precision multiply;   /* F16 or F32 (F8F143 has no B200 path) */
+    ipuc_precision accumulate; /* AccumulationPrecision: F32 on B200 */
+    uint32_t mode;             /* GemmKernelMode: 0 Initialize, 1 Accumulate */
+    uint32_t interleaved_weights; /* GemmWeightLoad::Interleaved (requires F16) */
+    uint32_t inner_block;      /* IPU K-block / output panel width: planning */
+    uint32_t output_columns;   /*   parameters, accepted and not used on B200 */
+    uint32_t b_transposed;     /* B200: right operand stored [n x k] */
+    uint32_t epilogue_gelu;    /* B200: fused GELU epilogue (graph lowering) */
+  } gemm;
+  struct { uint16_t partials; } reduction_sum; /* ReductionSum (>= 2) */
+  struct {                                      /* FlashAttention */
+    uint32_t causal;                            /* rejected, as operator.rs:997 */
+    float scale;                                /* <= 0: 1/sqrt(query width) */
+    ipuc_precision accumulate;
+  } flash_attention;
+  struct { uint32_t head_dimension, key_columns, padded_key_columns; } attention_softmax;
+  struct {
+    uint32_t value_dimension, padded_value_dimension, key_block_columns;
+    uint32_t initial, final_block;
+  } attention_merge;
+  struct { ipuc_precision from, to; } cast;
+  struct { ipuc_layout from, to; } rearrange;
+} ipuc_kernel_spec;
+
+/* A single-view operand (KernelOperand with one view): a dense row-major
+ * device tensor of up to 4 dims. */
+typedef struct {
+  void *data;
+  ipuc_precision precision;
+  int32_t rank;
+  int64_t dims[4];
+} ipuc_tensor;
+
+/* KernelAvailability: IMPLEMENTED has a B200 kernel; REQUIRED names a call
+ * the reference plans but nothing executes (ipuc_launch returns
+ * IPUC_ERR_UNSUPPORTED). */
+typedef enum { IPUC_AVAILABILITY_IMPLEMENTED = 0, IPUC_AVAILABILITY_REQUIRED = 1 } ipuc_availability;
+
+typedef struct {
+  const char *symbol;           /* the ipuc_* entry the call routes to */
+  const char *reference_symbol; /* the reference tile-kernel family it replaces */
+  ipuc_availability availability;
+  int32_t input_count;          /* pointer operands after the output (m3..) */
+  int32_t scalar_count;
+  const char *scalar_names[8];  /* kernel.rs:1149-1193 names, in call order */
+} ipuc_kernel_abi;
+
+/* tile_kernel_abi for one spec and the output precision
+ * (KernelRequirements::output.format.precision).  Pure host logic: touches
+ * no device.  IPUC_ERR_INVALID_ARGUMENT = KernelAbiError::RequirementMismatch. */
+ipuc_status ipuc_query_abi(const ipuc_kernel_spec *spec, ipuc_precision output_precision, ipuc_kernel_abi *abi);
+
+/* validate_kernel_run + the call.  `scalars` are the u32 values in the ABI's
+ * scalar order, as the reference derives them from the run; they must agree
+ * with the tensors.  Operand roles per kind:
+ *   FILL_ZERO      out; scalars words_per_worker, remainder_workers (bytes/8 = 6w + r)
+ *   GEMM           out C[m,n] (or [b,m,n]); in A[m,k], B[k,n] ([n,k] if b_transposed);
+ *                  F32 multiply needs `workspace` of ipuc_gemm_f32_workspace_bytes
+ *   GELU           out, in (f16); scalars element_count (even)
+ *   REDUCTION_SUM  out f16; in initial[count], remote[(partials-1) * count] (f16 or f32);
+ *                  scalars num_partials (= partials - 1), element_count (% 8 == 0)
+ *   ADD            out, left, right (f16); scalars element_count, left/right broadcast stride
+ *   FLASH_ATTENTION out[M,Sq,D] (f16 or f32); in Q[M,Sq,D], K[M,Sk,D], V[M,Sk,D] f16
+ *   ATTENTION_SOFTMAX out weights (+ f32 state); in scores [padded_key_columns/16][rows][16]
+ *   ATTENTION_MERGE out acc f32 [rows][padded_value_dimension]; in PV block, softmax
+ *                  weights buffer (state after key_block_columns * rows f16);
+ *                  scalars initial_block, final_block (must match the spec)
+ *   CAST           out, in; scalars element_count
+ *   REARRANGE      row-major -> AMP-Left/AMP-TransposedRight/BlockMajor: scalars
+ *                  logical_rows, physical_rows, target_order, logical_columns,
+ *                  physical_columns; AMP-Output/AMP-TransposedLeft -> row-major:
+ *                  matrices, logical_rows, physical_rows, logical_columns,
+ *                  physical_columns; any other pair: no scalars, [matrices, rows, cols].
+ * Errors mirror KernelAbiError: PointerArity / scalar arity and the count
+ * divisibility checks -> IPUC_ERR_INVALID_ARGUMENT with the reference's
+ * message; REQUIRED availability -> IPUC_ERR_UNSUPPORTED.  Nothing is
+ * launched when a check fails. */
+ipuc_status ipuc_launch(const ipuc_kernel_spec *spec, const ipuc_tensor *output, const ipuc_tensor *inputs,
+                        int32_t input_count, const uint32_t *scalars, int32_t scalar_count, void *workspace,
+                        uint64_t workspace_bytes, ipuc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,8 @@ SIGNATURES = {
     "ipuc_convert_order_f16": (_i32, [_vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _vp]),
     "ipuc_split_heads_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ipuc_merge_heads_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "ipuc_query_abi": (_i32, [_vp, _i32, _vp]),
+    "ipuc_launch": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _vp, _u64, _vp]),
 }
 
 
@@ -225,3 +227,179 @@ def split_heads_f16(out, inp, batch, rows, heads, channels, stream=None):
 
 def merge_heads_f16(out, inp, batch, rows, heads, channels, stream=None):
     call("ipuc_merge_heads_f16", _ptr(out), _ptr(inp), batch, rows, heads, channels, _stream(stream))
+
+
+# ---- spec-driven dispatch (ipuc_query_abi / ipuc_launch) -------------------
+# Mirrors TileKernelSpec (crates/ipu-codegen/src/operator.rs:57-96) and the
+# KernelAbi that tile_kernel_abi derives from it (kernel.rs:1215-1382).
+
+(KERNEL_FILL_ZERO, KERNEL_GEMM, KERNEL_GELU, KERNEL_REDUCTION_SUM, KERNEL_ADD, KERNEL_FLASH_ATTENTION,
+ KERNEL_ATTENTION_SOFTMAX, KERNEL_ATTENTION_MERGE, KERNEL_CAST, KERNEL_REARRANGE) = range(10)
+AVAILABILITY_IMPLEMENTED, AVAILABILITY_REQUIRED = 0, 1
+
+
+class Layout(ctypes.Structure):
+    _fields_ = [("order", ctypes.c_int32), ("row_block", ctypes.c_uint32), ("column_block", ctypes.c_uint32)]
+
+
+class _Gemm(ctypes.Structure):
+    _fields_ = [("multiply", ctypes.c_int32), ("accumulate", ctypes.c_int32), ("mode", ctypes.c_uint32),
+                ("interleaved_weights", ctypes.c_uint32), ("inner_block", ctypes.c_uint32),
+                ("output_columns", ctypes.c_uint32), ("b_transposed", ctypes.c_uint32),
+                ("epilogue_gelu", ctypes.c_uint32)]
+
+
+class _Reduction(ctypes.Structure):
+    _fields_ = [("partials", ctypes.c_uint16)]
+
+
+class _Attention(ctypes.Structure):
+    _fields_ = [("causal", ctypes.c_uint32), ("scale", ctypes.c_float), ("accumulate", ctypes.c_int32)]
+
+
+class _Softmax(ctypes.Structure):
+    _fields_ = [("head_dimension", ctypes.c_uint32), ("key_columns", ctypes.c_uint32),
+                ("padded_key_columns", ctypes.c_uint32)]
+
+
+class _Merge(ctypes.Structure):
+    _fields_ = [("value_dimension", ctypes.c_uint32), ("padded_value_dimension", ctypes.c_uint32),
+                ("key_block_columns", ctypes.c_uint32), ("initial", ctypes.c_uint32), ("final_block", ctypes.c_uint32)]
+
+
+class _Cast(ctypes.Structure):
+    _fields_ = [("from_", ctypes.c_int32), ("to", ctypes.c_int32)]
+
+
+class _Rearrange(ctypes.Structure):
+    _fields_ = [("from_", Layout), ("to", Layout)]
+
+
+class KernelSpec(ctypes.Structure):
+    """ipuc_kernel_spec; build one with the TileKernelSpec-named helpers below."""
+    _fields_ = [("kind", ctypes.c_int32), ("gemm", _Gemm), ("reduction_sum", _Reduction),
+                ("flash_attention", _Attention), ("attention_softmax", _Softmax), ("attention_merge", _Merge),
+                ("cast", _Cast), ("rearrange", _Rearrange)]
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("precision", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("dims", ctypes.c_int64 * 4)]
+
+
+class KernelAbi(ctypes.Structure):
+    _fields_ = [("symbol", ctypes.c_char_p), ("reference_symbol", ctypes.c_char_p), ("availability", ctypes.c_int32),
+                ("input_count", ctypes.c_int32), ("scalar_count", ctypes.c_int32),
+                ("scalar_names", ctypes.c_char_p * 8)]
+
+
+def _layout(order, row_block=0, column_block=0):
+    if isinstance(order, Layout):
+        return order
+    return Layout(order, row_block, column_block)
+
+
+class TileKernelSpec:
+    """Constructors named after the reference enum's variants."""
+
+    @staticmethod
+    def fill_zero():
+        return KernelSpec(kind=KERNEL_FILL_ZERO)
+
+    @staticmethod
+    def gemm(multiply=F16, accumulate=F32, mode="initialize", interleaved_weights=False, inner_block=64,
+             output_columns=16, b_transposed=False, epilogue_gelu=False):
+        s = KernelSpec(kind=KERNEL_GEMM)
+        s.gemm = _Gemm(multiply, accumulate, 1 if mode == "accumulate" else 0, int(interleaved_weights),
+                       inner_block, output_columns, int(b_transposed), int(epilogue_gelu))
+        return s
+
+    @staticmethod
+    def gelu():
+        return KernelSpec(kind=KERNEL_GELU)
+
+    @staticmethod
+    def reduction_sum(partials):
+        s = KernelSpec(kind=KERNEL_REDUCTION_SUM)
+        s.reduction_sum = _Reduction(partials)
+        return s
+
+    @staticmethod
+    def add():
+        return KernelSpec(kind=KERNEL_ADD)
+
+    @staticmethod
+    def flash_attention(causal=False, scale=0.0, accumulate=F32):
+        s = KernelSpec(kind=KERNEL_FLASH_ATTENTION)
+        s.flash_attention = _Attention(int(causal), scale, accumulate)
+        return s
+
+    @staticmethod
+    def attention_softmax(head_dimension, key_columns, padded_key_columns):
+        s = KernelSpec(kind=KERNEL_ATTENTION_SOFTMAX)
+        s.attention_softmax = _Softmax(head_dimension, key_columns, padded_key_columns)
+        return s
+
+    @staticmethod
+    def attention_merge(value_dimension, padded_value_dimension, key_block_columns, initial, final_block):
+        s = KernelSpec(kind=KERNEL_ATTENTION_MERGE)
+        s.attention_merge = _Merge(value_dimension, padded_value_dimension, key_block_columns, int(initial),
+                                   int(final_block))
+        return s
+
+    @staticmethod
+    def cast(frm, to):
+        s = KernelSpec(kind=KERNEL_CAST)
+        s.cast = _Cast(frm, to)
+        return s
+
+    @staticmethod
+    def rearrange(frm, to):
+        s = KernelSpec(kind=KERNEL_REARRANGE)
+        s.rearrange = _Rearrange(_layout(*frm) if isinstance(frm, tuple) else _layout(frm),
+                                 _layout(*to) if isinstance(to, tuple) else _layout(to))
+        return s
+
+
+def _precision_of(t):
+    import torch
+    if t.dtype == torch.float16:
+        return F16
+    if t.dtype == torch.float32:
+        return F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def tensor(t, shape=None, precision=None):
+    """ipuc_tensor for a torch tensor (dense; `shape` overrides its shape)."""
+    shape = tuple(t.shape) if shape is None else tuple(shape)
+    if not 1 <= len(shape) <= 4:
+        raise ValueError("rank 1..4")
+    dims = (ctypes.c_int64 * 4)(*(list(shape) + [0] * (4 - len(shape))))
+    out = Tensor(t.data_ptr(), _precision_of(t) if precision is None else precision, len(shape), dims)
+    out._owner = t  # keep the device memory alive as long as the descriptor
+    return out
+
+
+def query_abi(spec, output_precision=F16):
+    """tile_kernel_abi: dict(symbol, reference_symbol, availability, input_count, scalar_names)."""
+    abi = KernelAbi()
+    call("ipuc_query_abi", ctypes.byref(spec), output_precision, ctypes.byref(abi))
+    return {
+        "symbol": abi.symbol.decode(),
+        "reference_symbol": abi.reference_symbol.decode(),
+        "availability": abi.availability,
+        "input_count": abi.input_count,
+        "scalar_names": [abi.scalar_names[i].decode() for i in range(abi.scalar_count)],
+    }
+
+
+def launch(spec, out, inputs=(), scalars=(), workspace=None, stream=None):
+    """validate_kernel_run + call: `out`/`inputs` are torch tensors or Tensor structs."""
+    o = out if isinstance(out, Tensor) else tensor(out)
+    ins = [x if isinstance(x, Tensor) else tensor(x) for x in inputs]
+    arr = (Tensor * max(1, len(ins)))(*ins) if ins else None
+    sc = (ctypes.c_uint32 * max(1, len(scalars)))(*scalars) if scalars else None
+    ws = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    call("ipuc_launch", ctypes.byref(spec), ctypes.byref(o), arr, len(ins), sc, len(scalars), _ptr(workspace), ws,
+         _stream(stream))
