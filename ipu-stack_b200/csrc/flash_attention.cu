@@ -295,8 +295,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         l *= alpha;
       }
       // P = 2^(s*c - m*c) in packed f16 written to S columns [h*32, h*32+32):
-      // packed f32x2 arithmetic, one pair in four exponentiated on the FMA
-      // pipe (exp2_poly2) to unload the MUFU unit.  Masked keys hold -inf -> 0.
+      // packed f32x2 arithmetic, one pair in three exponentiated on the FMA
+      // pipe (exp2_poly2) to unload the MUFU unit (16 ex2 per clock per SM;
+      // a third on the polynomial balances it against the FMA pipe).  Masked
+      // keys hold -inf -> 0.
       const float mc = m * c;
       const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
       uint64_t sum2 = f2_pack(0.0f, 0.0f);
@@ -307,7 +309,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
         const uint64_t tt = f2_fma(f2_pack(x0, x1), c2, nmc2);
         uint64_t pp;
-        if ((i & 3) == 3) {
+        if ((i % 3) == 2) {
           pp = exp2_poly2(tt);
         } else {
           float t0, t1;

@@ -177,6 +177,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t
       : "memory");
 }
 // 32 lanes x 32 columns store (registers -> tensor memory).
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -203,6 +211,16 @@ __device__ __forceinline__ void tmem_regs_fence(uint32_t (&r)[32]) {
                  "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
 }
 __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  tmem_wait_ld();
+  tmem_regs_fence(r);
+}
+__device__ __forceinline__ void tmem_regs_fence(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]));
+}
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
   tmem_wait_ld();
   tmem_regs_fence(r);
 }
@@ -332,8 +350,13 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t t) {
   float p0, p1, y0, y1;
   f2_unpack(p, p0, p1);
   f2_unpack(y, y0, y1);
-  const uint32_t r0 = __float_as_uint(y0) * 8388608u + __float_as_uint(p0);
-  const uint32_t r1 = __float_as_uint(y1) * 8388608u + __float_as_uint(p1);
+  // Exponent insert with shift + add (integer ALU pipe) rather than a multiply-add,
+  // which would compete with the polynomial for the FMA pipe.
+  uint32_t r0, r1;
+  asm("shl.b32 %0, %1, 23;" : "=r"(r0) : "r"(__float_as_uint(y0)));
+  asm("shl.b32 %0, %1, 23;" : "=r"(r1) : "r"(__float_as_uint(y1)));
+  asm("add.u32 %0, %0, %1;" : "+r"(r0) : "r"(__float_as_uint(p0)));
+  asm("add.u32 %0, %0, %1;" : "+r"(r1) : "r"(__float_as_uint(p1)));
   return f2_pack(__uint_as_float(r0), __uint_as_float(r1));
 }
 
