@@ -222,16 +222,64 @@ def run_ours(args):
         h.copy_(d)
     torch.cuda.synchronize()
 
+    # The step is pipelined over three streams: host->device copies (s_in),
+    # the kernels (the bench stream) and device->host copies (s_out), chunked
+    # so that each chunk's kernel starts when its inputs have landed and its
+    # result leaves while later chunks are still arriving (PCIe is full duplex).
+    # W goes first (every GEMM chunk reads all of it), then X in row chunks,
+    # then Q/K/V in stream chunks.  One device buffer set serves every step:
+    # a chunk's upload waits for the previous step's kernel on that chunk, and
+    # a kernel waits for the previous step's read-back of its output chunk.
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    g_chunks = [(r, min(MLP_M, r + MLP_M // 4)) for r in range(0, MLP_M, MLP_M // 4)]
+    a_step = max(1, ns // 8)
+    a_chunks = [(c, min(ns, c + a_step)) for c in range(0, ns, a_step)]
+    n_ch = len(g_chunks) + len(a_chunks)
+    in_ev = [torch.cuda.Event() for _ in range(n_ch)]
+    comp_ev = [torch.cuda.Event() for _ in range(n_ch)]
+    out_ev = [torch.cuda.Event() for _ in range(n_ch)]
+    w_ev = torch.cuda.Event()
+
     def e2e_step():
-        x.copy_(hx, non_blocking=True)
-        w.copy_(hw, non_blocking=True)
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        gemm()
-        attn()
-        hy.copy_(y, non_blocking=True)
-        ho.copy_(o, non_blocking=True)
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(comp_ev[len(g_chunks) - 1])  # previous step's GEMMs are done with W
+            w.copy_(hw, non_blocking=True)
+            w_ev.record(s_in)
+            for i, (r0, r1) in enumerate(g_chunks):
+                s_in.wait_event(comp_ev[i])
+                x[r0:r1].copy_(hx[r0:r1], non_blocking=True)
+                in_ev[i].record(s_in)
+            for j, (c0, c1) in enumerate(a_chunks):
+                i = len(g_chunks) + j
+                s_in.wait_event(comp_ev[i])
+                q[c0:c1].copy_(hq[c0:c1], non_blocking=True)
+                k[c0:c1].copy_(hk[c0:c1], non_blocking=True)
+                v[c0:c1].copy_(hv[c0:c1], non_blocking=True)
+                in_ev[i].record(s_in)
+        stream.wait_event(w_ev)
+        for i, (r0, r1) in enumerate(g_chunks):
+            stream.wait_event(in_ev[i])
+            stream.wait_event(out_ev[i])
+            ipuc.call("ipuc_gemm_f16", y[r0].data_ptr(), x[r0].data_ptr(), w.data_ptr(), r1 - r0, nw, MLP_K, MLP_K,
+                      nw, nw, ipuc.GEMM_EPILOGUE_GELU, s)
+            comp_ev[i].record(stream)
+        for j, (c0, c1) in enumerate(a_chunks):
+            i = len(g_chunks) + j
+            stream.wait_event(in_ev[i])
+            stream.wait_event(out_ev[i])
+            ipuc.call("ipuc_flash_attention_f16", o[c0].data_ptr(), ipuc.F16, q[c0].data_ptr(), k[c0].data_ptr(),
+                      v[c0].data_ptr(), c1 - c0, ATT_S, ATT_S, ATT_D, 0.0, s)
+            comp_ev[i].record(stream)
+        with torch.cuda.stream(s_out):
+            for i, (r0, r1) in enumerate(g_chunks):
+                s_out.wait_event(comp_ev[i])
+                hy[r0:r1].copy_(y[r0:r1], non_blocking=True)
+                out_ev[i].record(s_out)
+            for j, (c0, c1) in enumerate(a_chunks):
+                i = len(g_chunks) + j
+                s_out.wait_event(comp_ev[i])
+                ho[c0:c1].copy_(o[c0:c1], non_blocking=True)
+                out_ev[i].record(s_out)
 
     e2e_steps = max(1, min(args.steps, 5))
     for _ in range(2):
@@ -240,8 +288,11 @@ def run_ours(args):
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
     for _ in range(e2e_steps):
         e2e_step()
+    stream.wait_event(out_ev[-1])
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
