@@ -40,6 +40,9 @@ constexpr int HALF_BYTES = TILE_BYTES / 2;
 constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
 constexpr int NUM_THREADS = 576;  // 2 + 16 warps
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+// The split merge's receive area (2*TQ padded O rows + m and l) must fit in
+// the Q/K/V tiles it reuses.
+static_assert((2 * TQ * (DP + 4) + 4 * TQ) * 4 <= 6 * TILE_BYTES, "split merge area");
 
 struct AttnParams {
   void *out;
@@ -47,6 +50,8 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   int32_t out_f32;
   int32_t key_tiles;
+  int32_t q_units;    // query units per stream: 512-row (pair, split) or 256-row blocks
+  int64_t unit_base;  // first unit of this launch (split: first 256-row half-unit)
   uint32_t *err;
 };
 
@@ -55,7 +60,13 @@ struct AttnParams {
 // every K tile (64 keys) and of every V tile (64 head-dim columns), halving
 // per-CTA shared-memory fill and B-operand reads; the leader (rank 0) issues
 // all MMAs and both CTAs' softmax warps run as in the single-CTA kernel.
-template <bool kPair>
+// kSplit: the tail of a pair launch.  Each 2-CTA cluster owns one 256-row
+// unit; CTA r runs key tiles [r*ceil(n/2), ...) of it, and CTA 1 hands its
+// unnormalised O, running max and row sum to CTA 0 through distributed shared
+// memory for the merge (the two-block case of the merge stage's rescale,
+// device/attention_stages_f16.S:803-849).  Used when the pair units leave a
+// last wave less than half full, so the split halves that wave's length.
+template <bool kPair, bool kSplit>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -75,19 +86,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t *v_empty = bars + 12; // [2] V stage free (its PV products done)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint64_t *merge_ready = bars + 15;  // split, CTA 1: CTA 0's tiles are free to receive
+  uint64_t *merge_full = bars + 16;   // split, CTA 0: CTA 1's partial has landed
 
   __shared__ float xmax[2][2][TQ], xsum[2][2][TQ];  // [tile][column half][row]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t stream = blockIdx.y;
-  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
-  const bool leader = rank == 0;
-  const int32_t q0 = kPair ? (int32_t)(blockIdx.x >> 1) * (4 * TQ) + (int32_t)rank * (2 * TQ)
-                           : (int32_t)blockIdx.x * (2 * TQ);
+  const uint32_t rank = (kPair || kSplit) ? cluster_ctarank() : 0u;
+  const uint32_t prank = kPair ? rank : 0u;  // half of K/V this CTA loads (pair only)
+  const bool leader = prank == 0;
+  int64_t stream;
+  int32_t q0;
+  if (kPair) {
+    const int64_t u = p.unit_base + (blockIdx.x >> 1);
+    stream = u / p.q_units;
+    q0 = (int32_t)(u % p.q_units) * (4 * TQ) + (int32_t)rank * (2 * TQ);
+  } else if (kSplit) {
+    const int64_t u = p.unit_base + (blockIdx.x >> 1), pu = u >> 1;
+    stream = pu / p.q_units;
+    q0 = (int32_t)(pu % p.q_units) * (4 * TQ) + (int32_t)(u & 1) * (2 * TQ);
+  } else {
+    const int64_t u = p.unit_base + blockIdx.x;
+    stream = u / p.q_units;
+    q0 = (int32_t)(u % p.q_units) * (2 * TQ);
+  }
   constexpr int K_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA K tile (64 or 128 keys)
   constexpr int K_HALF = K_BYTES / 2;                             // one 64-column head-dim half
   constexpr int V_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA V tile (64 or 128 D columns)
   constexpr int TX_MULT = kPair ? 2 : 1;                          // leader counts both CTAs' bytes
-  const int n_tiles = p.key_tiles;
+  // Key tiles [j_begin, j_begin + n_tiles) of the stream; loop counters below
+  // are local (they set stage and phase), key coordinates add j_begin.
+  const int split_half = (p.key_tiles + 1) / 2;
+  const int j_begin = kSplit ? (int)rank * split_half : 0;
+  const int n_tiles = kSplit ? min(p.key_tiles - j_begin, split_half) : p.key_tiles;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -100,6 +130,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&p_ready[i], kPair ? 16 : 8);  // lane 0 of each softmax warp of the tile
     }
     mbar_init(o_final, 1);
+    mbar_init(merge_ready, 1);
+    mbar_init(merge_full, 16 * 32);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmQ);
@@ -116,7 +148,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
   tc_fence_before();
-  if (kPair) cluster_sync();
+  if (kPair || kSplit) cluster_sync();
   else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -140,16 +172,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (leader) mbar_arrive_expect_tx(&k_full[st], TX_MULT * K_BYTES);
         for (int h = 0; h < 2; ++h)
-          load(sK + st * TILE_BYTES + h * K_HALF, &tmK, &k_full[st], h * 64, j * TK + (int32_t)rank * (TK / 2));
+          load(sK + st * TILE_BYTES + h * K_HALF, &tmK, &k_full[st], h * 64,
+               (j_begin + j) * TK + (int32_t)prank * (TK / 2));
         if (!mbar_wait_bounded(&v_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
         if (leader) mbar_arrive_expect_tx(&v_full[st], TX_MULT * V_BYTES);
         if (kPair) {
-          load(sV + st * TILE_BYTES, &tmV, &v_full[st], (int32_t)rank * 64, j * TK);
+          load(sV + st * TILE_BYTES, &tmV, &v_full[st], (int32_t)prank * 64, (j_begin + j) * TK);
         } else {
-          for (int h = 0; h < 2; ++h) load(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, j * TK);
+          for (int h = 0; h < 2; ++h)
+            load(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, (j_begin + j) * TK);
         }
       }
       if (!ok) {
@@ -252,7 +286,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const int64_t rem_keys = p.sk - (int64_t)j * TK - h * 64;
+      const int64_t rem_keys = p.sk - (int64_t)(j_begin + j) * TK - h * 64;
       const int valid = rem_keys < 64 ? (rem_keys > 0 ? (int)rem_keys : 0) : 64;
       // This warp's 64 scores stay in registers (P overwrites S columns of the
       // partner's half only after the barrier below).
@@ -355,14 +389,72 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (ok && mbar_wait_bounded(o_final, 0, abort_flag)) {
       tc_fence_after();
       const int64_t grow = (int64_t)q0 + t * TQ + row;
-      const float inv = 1.0f / l;
       const bool row_ok = grow < p.sq;
       const int64_t base = (stream * p.sq + grow) * p.d;
+      // Split merge area in CTA 0: its Q/K/V tiles, dead once its MMAs are
+      // complete.  Rows are padded to RECV_LD floats so that one warp's
+      // float4 reads of 32 rows spread over all banks.
+      constexpr int RECV_LD = DP + 4;
+      float *recv_o = reinterpret_cast<float *>(smem);
+      float *recv_m = recv_o + 2 * TQ * RECV_LD, *recv_l = recv_m + 2 * TQ;
+      const int r2 = t * TQ + row;
+      float a_own = 1.0f, a_peer = 0.0f;
+      bool store = true;
+      if (kSplit && rank == 1) {
+        // Ship this CTA's unnormalised O (64 columns per thread), m and l.
+        store = false;
+        if (!mbar_wait_cluster_bounded(merge_ready, 0, abort_flag)) {
+          ok = false;
+        } else {
+          const uint32_t dst = map_shared_rank(smem_u32(recv_o + (size_t)r2 * RECV_LD + h * 64), 0);
 #pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
+          for (int ch = 0; ch < 2; ++ch) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_col + ch * 32, r);
+            tmem_wait_ld(r);
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              st_cluster_v4(dst + (uint32_t)(ch * 32 + i) * 4u, __uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                            __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+          }
+          if (h == 0) {
+            st_cluster_f32(map_shared_rank(smem_u32(recv_m + r2), 0), m);
+            st_cluster_f32(map_shared_rank(smem_u32(recv_l + r2), 0), l);
+          }
+          mbar_arrive_cluster(map_shared_rank(smem_u32(merge_full), 0));
+        }
+      } else if (kSplit) {
+        // CTA 0: release the tiles to CTA 1, wait for its partial, rescale
+        // both halves to the larger running max.
+        if (warp == 2 && lane == 0) mbar_arrive_cluster(map_shared_rank(smem_u32(merge_ready), 1));
+        if (!mbar_wait_cluster_bounded(merge_full, 0, abort_flag)) {
+          ok = false;
+          store = false;
+        } else {
+          const float m_peer = recv_m[r2], l_peer = recv_l[r2];
+          const float mf = fmaxf(m, m_peer);
+          a_own = ex2_approx((m - mf) * c);
+          a_peer = ex2_approx((m_peer - mf) * c);
+          l = l * a_own + l_peer * a_peer;
+        }
+      }
+      const float inv = 1.0f / l;
+      const float *peer = recv_o + (size_t)r2 * RECV_LD + h * 64;
+#pragma unroll
+      for (int ch = 0; ch < 2 && store; ++ch) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(o_col + ch * 32, r);
         tmem_wait_ld(r);
+        if (kSplit) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(peer + ch * 32 + i);
+            r[i] = __float_as_uint(__uint_as_float(r[i]) * a_own + q4.x * a_peer);
+            r[i + 1] = __float_as_uint(__uint_as_float(r[i + 1]) * a_own + q4.y * a_peer);
+            r[i + 2] = __float_as_uint(__uint_as_float(r[i + 2]) * a_own + q4.z * a_peer);
+            r[i + 3] = __float_as_uint(__uint_as_float(r[i + 3]) * a_own + q4.w * a_peer);
+          }
+        }
         const int col0 = h * 64 + ch * 32;
         if (!row_ok || col0 >= p.d) continue;
         if (p.out_f32) {
@@ -393,7 +485,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (kPair) cluster_sync();
+  if (kPair || kSplit) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     if (kPair) tmem_dealloc_pair(tmem, 512);
@@ -422,7 +514,7 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
                  "flash_attention: extent too large");
   // CTA pairs when every pair gets a full 512-row query block.
   const bool pair = query_rows >= 4 * TQ;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tk_full;
   ipuc_status st = make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q, head_dim, query_rows, matrices, head_dim,
                                query_rows * head_dim, 64, TQ);
   if (st != IPUC_OK) return st;
@@ -442,11 +534,12 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
   p.scale_log2 = s * 1.4426950408889634f;
   p.out_f32 = out_precision == IPUC_F32;
   p.key_tiles = (int32_t)((key_rows + TK - 1) / TK);
+  p.unit_base = 0;
   p.err = device_error_word();
-  if (pair) {
-    IPUC_CUDA(cudaFuncSetAttribute(flash_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  auto launch = [&](auto kernel, int64_t ctas, bool cluster, const CUtensorMap &kmap) -> ipuc_status {
+    IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(2 * ((query_rows + 4 * TQ - 1) / (4 * TQ))), (unsigned)matrices);
+    cfg.gridDim = dim3((unsigned)ctas);
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = SMEM_BYTES;
     cfg.stream = stream;
@@ -456,12 +549,31 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    IPUC_CUDA(cudaLaunchKernelEx(&cfg, flash_attention_kernel<true>, tq, tk, tv, p));
-  } else {
-    IPUC_CUDA(cudaFuncSetAttribute(flash_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    dim3 grid((unsigned)((query_rows + 2 * TQ - 1) / (2 * TQ)), (unsigned)matrices);
-    flash_attention_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+    cfg.numAttrs = cluster ? 1 : 0;
+    IPUC_CUDA(cudaLaunchKernelEx(&cfg, kernel, tq, kmap, tv, p));
+    return check_launch("flash_attention_kernel");
+  };
+  if (!pair) {
+    p.q_units = (int32_t)((query_rows + 2 * TQ - 1) / (2 * TQ));
+    return launch(flash_attention_kernel<false, false>, matrices * p.q_units, false, tk);
   }
-  return check_launch("flash_attention_kernel");
+  // Pair units of 512 query rows.  When they leave a last wave at most half
+  // full, that tail runs as split clusters (two CTAs per 256-row unit, each
+  // over half the keys), which halves the tail wave's length.
+  p.q_units = (int32_t)((query_rows + 4 * TQ - 1) / (4 * TQ));
+  const int64_t units = matrices * p.q_units, slots = sm_count() / 2;
+  const int64_t tail = units % slots, full = units - tail;
+  const bool split = tail > 0 && 4 * tail <= 2 * slots && p.key_tiles >= 2;
+  const int64_t paired = split ? full : units;
+  if (paired > 0) {
+    st = launch(flash_attention_kernel<true, false>, 2 * paired, true, tk);
+    if (st != IPUC_OK) return st;
+  }
+  if (!split) return IPUC_OK;
+  st = make_map_3d(&tk_full, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, k, head_dim, key_rows, matrices, head_dim,
+                   key_rows * head_dim, 64, TK);
+  if (st != IPUC_OK) return st;
+  p.unit_base = 2 * full;  // 256-row half-units
+  return launch(flash_attention_kernel<false, true>, 4 * tail, true, tk_full);
 }
+

@@ -76,6 +76,38 @@ def test_attention_rescale_path():
     assert ok, msg
 
 
+@pytest.mark.parametrize("M,Sq,Sk,D", [
+    (38, 1024, 300, 128),   # 76 pair units on 74 pair slots: one full pair wave + a 2-unit split tail
+    (35, 1024, 256, 64),    # 70 pair units: last wave more than half full, pairs only
+    (3, 700, 1000, 128),    # 6 units, all split; ragged query rows inside a unit
+])
+def test_attention_pair_and_split_tail(M, Sq, Sk, D):
+    """Launch partition on B200's 148 SMs: 512-row pair units fill whole waves;
+    a tail of at most half a wave runs as split clusters (each 256-row unit
+    over two CTAs holding half the keys, merged through shared memory)."""
+    q, k, v = inputs(M + Sq + Sk, M, Sq, Sk, D)
+    got = run(q, k, v, out_f32=False)
+    ref = oracle.quantize_f16(oracle.attention(f16_of(q), f16_of(k), f16_of(v), threads=8))
+    ok, msg = f16_close(got, ref)
+    assert ok, msg
+
+
+def test_attention_split_merge_rescale():
+    """Split halves with very different running maxima: the merge rescales both
+    partial sums to the larger max (attention_stages_f16.S:803-829)."""
+    M, Sq, Sk, D = 1, 512, 1024, 128
+    rng = np.random.default_rng(5)
+    qf = rng.standard_normal((M, Sq, D)).astype(np.float32) * 0.5
+    ramp = np.linspace(0.1, 4.0, Sk, dtype=np.float32)[None, :, None]
+    kf = (np.abs(rng.standard_normal((M, Sk, D))).astype(np.float32) * ramp) * np.sign(qf.mean(axis=1, keepdims=True))
+    vf = rng.standard_normal((M, Sk, D)).astype(np.float32)
+    q, k, v = oracle.f16_bits(qf), oracle.f16_bits(kf), oracle.f16_bits(vf)
+    got = run(q, k, v, out_f32=True)
+    ref = oracle.attention(f16_of(q), f16_of(k), f16_of(v))
+    ok, msg = f16_close(got, ref)
+    assert ok, msg
+
+
 def test_attention_custom_scale():
     q, k, v = inputs(11, 2, 200, 300, 128)
     got = run(q, k, v, out_f32=True, scale=0.02)
