@@ -340,7 +340,8 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1), "peak": peak_sus,
                          "unit": "TFLOP/s", "frac": round(achieved / peak_sus, 4),
                          "peak_kind": f"{peak_kind} bf16 sustained", "frac_of_burst": round(achieved / peak_burst, 4),
-                         "traffic": profiled_traffic(dom)},
+                         "traffic": profiled_traffic(dom, ns / (ATT_B * ATT_H) if dom == "flash_attention"
+                                                     else nw / MLP_N)},
             "kernels": {"gemm_f16_gelu": {"ms": round(gemm_ms, 4),
                                           "tflops": round(GEMM_FLOP * nw / MLP_N / (gemm_ms * 1e-3) / 1e12, 1)},
                         "flash_attention": {"ms": round(attn_ms, 4),
@@ -354,12 +355,15 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def profiled_traffic(kernel: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+def profiled_traffic(kernel: str, share: float = 1.0):
+    """DRAM bytes per launch from the committed ncu summary (captured on the
+    full single-GPU launch), scaled to this rank's shard of the work, which
+    traffic grows in proportion to; None without a summary."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(path):
         with open(path) as f:
-            return json.load(f).get(kernel)
+            v = json.load(f).get(kernel)
+        return None if v is None else int(round(v * share))
     return None
 
 
@@ -560,8 +564,9 @@ def profile_case(kernel: str):
         c = torch.empty((m, n), device="cuda", dtype=torch.float16)
         run = lambda: ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n,
                                 ipuc.GEMM_EPILOGUE_GELU, s)
-    elif kernel == "attention":
-        M = ATT_B * ATT_H
+    elif kernel in ("attention", "attention8"):
+        # attention8: the 8-GPU shard (32 streams), whose tail runs as split clusters.
+        M = ATT_B * ATT_H if kernel == "attention" else ATT_B * ATT_H // 8
         q, kk, v = (torch.randn((M, ATT_S, ATT_D), device="cuda").half() for _ in range(3))
         o = torch.empty_like(q)
         run = lambda: ipuc.call("ipuc_flash_attention_f16", o.data_ptr(), ipuc.F16, q.data_ptr(), kk.data_ptr(),
@@ -596,7 +601,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
-    ap.add_argument("--profile", choices=["gemm", "attention", "rearrange", "rearrange_amp_left", "gemm_f32"],
+    ap.add_argument("--profile", choices=["gemm", "attention", "attention8", "rearrange", "rearrange_amp_left",
+                                          "gemm_f32"],
                     help="run a few launches of one kernel on a small case (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile:
