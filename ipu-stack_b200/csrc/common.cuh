@@ -44,6 +44,7 @@ enum : uint32_t {
   ERR_KERNEL_GEMM_TF32 = 2u << 16,
   ERR_KERNEL_ATTENTION = 3u << 16,
   ERR_KERNEL_SELFTEST = 4u << 16,
+  ERR_KERNEL_LAYOUT = 5u << 16,
 };
 
 __device__ __forceinline__ void record_device_error(uint32_t *word, uint32_t code) {

@@ -15,6 +15,8 @@
 // of the destination block.  Global traffic is one read and one write of
 // each byte in full 32-byte sectors (HBM-bound, no tensor cores).
 #include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
 
 namespace ipuc {
 namespace {
@@ -380,6 +382,111 @@ ipuc_status check_side(const Side &s, const char *which) {
   return fail(IPUC_ERR_INVALID_ARGUMENT, w + ": unknown element order");
 }
 
+// ---- Row-major -> BlockMajor{64,16}: TMA + ldmatrix.trans / stmatrix ------------
+// BlockMajor{64,16} (storage.rs:372-426) stores each 64-row band contiguously:
+// for every 16-column block, its four 16x16 row groups, each column-major.  A
+// 64x64 row-major tile therefore becomes 8 KB of contiguous output.  A TMA load
+// (128-byte swizzle: the 16-byte chunk j of tile row r sits at chunk j ^ (r % 8),
+// so the 8 row addresses of each ldmatrix hit distinct banks) brings the tile in;
+// ldmatrix.trans turns each 8x8 sub-matrix so that a lane holds one column's
+// two rows, which is exactly the fragment stmatrix writes as one output row
+// (the output's "rows" being the micro-block's columns); one bulk copy stores
+// the tile.  About a quarter of an instruction per element, against one or more
+// for lane-level transposes, so the kernel runs at HBM speed.
+constexpr int BM64_TILE_BYTES = 64 * 64 * 2;  // 8 KB
+constexpr int BM64_STAGES = 8;                // input tiles in flight per CTA
+constexpr int BM64_OUT = 3;                   // output tiles (bulk stores draining)
+constexpr int BM64_SMEM = (BM64_STAGES + BM64_OUT) * BM64_TILE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t &a, uint32_t &b, uint32_t &c, uint32_t &d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_store(void *gdst, uint32_t ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__global__ void __launch_bounds__(128, 2)
+    rm_to_block_major64_kernel(const __grid_constant__ CUtensorMap src_map, uint16_t *__restrict__ dst,
+                               int64_t tiles, int32_t band_tiles, int32_t bands, int64_t cols, uint32_t *err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *in = smem;
+  uint8_t *out = smem + BM64_STAGES * BM64_TILE_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(out + BM64_OUT * BM64_TILE_BYTES);
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BM64_STAGES; ++s) sm100::mbar_init(&full[s], 1);
+    abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::tma_prefetch_desc(&src_map);
+  }
+  __syncthreads();
+  // Tile t = (matrix * bands + band) * band_tiles + ct: 64 rows x 64 columns.
+  auto issue = [&](int64_t t, int s) {
+    const int64_t mb = t / band_tiles;
+    const int32_t ct = (int32_t)(t - mb * band_tiles);
+    const int32_t band = (int32_t)(mb % bands), m = (int32_t)(mb / bands);
+    sm100::mbar_arrive_expect_tx(&full[s], BM64_TILE_BYTES);
+    sm100::tma_load_3d(in + s * BM64_TILE_BYTES, &src_map, &full[s], ct * 64, band * 64, m);
+  };
+  if (threadIdx.x == 0)
+    for (int s = 0; s < BM64_STAGES; ++s) {
+      const int64_t t = blockIdx.x + (int64_t)s * gridDim.x;
+      if (t < tiles) issue(t, s);
+    }
+  // ldmatrix row addresses (lane -> sub-matrix i = lane / 8, row lane % 8) and
+  // stmatrix row addresses for this warp's row group g = warp.
+  const int i = lane >> 3, j = lane & 7, g = warp;
+  const int in_row = g * 16 + (i & 1) * 8 + j;  // in_row % 8 == j
+  const uint32_t out_row_off = (uint32_t)((((i >> 1) * 8 + j) * 16 + (i & 1) * 8) * 2);
+  uint32_t it = 0;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+    const int s = (int)(it % BM64_STAGES);
+    const bool ok = sm100::mbar_wait_bounded(&full[s], (it / BM64_STAGES) & 1u, &abort_flag);
+    const uint32_t src_tile = sm100::smem_u32(in + s * BM64_TILE_BYTES);
+    const uint32_t ob = sm100::smem_u32(out + (it % BM64_OUT) * BM64_TILE_BYTES);
+#pragma unroll
+    for (int b = 0; b < 4 && ok; ++b) {
+      // Micro-block (row group g, column block b): sub-matrix i covers rows
+      // (i & 1) * 8 and columns (i >> 1) * 8 of it.
+      const int chunk = b * 2 + (i >> 1);
+      uint32_t r0, r1, r2, r3;
+      ldmatrix_x4_trans(src_tile + (uint32_t)(in_row * 128 + ((chunk ^ j) << 4)), r0, r1, r2, r3);
+      stmatrix_x4(ob + (uint32_t)((b * 4 + g) * 256 * 2) + out_row_off, r0, r1, r2, r3);
+    }
+    sm100::fence_proxy_async_smem();  // the bulk copy (async proxy) reads what stmatrix wrote
+    // Tile consumed (stage s reusable, output tile complete); a timed-out wait
+    // anywhere in the CTA ends every thread's loop here together.
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) record_device_error(err, ERR_KERNEL_LAYOUT | ERR_SITE_PRODUCER);
+      break;
+    }
+    if (threadIdx.x == 0) {
+      const int64_t mb = t / band_tiles;
+      const int64_t ct = t - mb * band_tiles;
+      // Band mb (matrix-major) starts at mb * 64 * cols; column tile ct adds 4 blocks of 1024.
+      bulk_store(dst + mb * 64 * cols + ct * 4096, ob, BM64_TILE_BYTES);
+      bulk_wait_read_1();  // the store issued one tile ago has read its buffer
+      const int64_t next = t + (int64_t)BM64_STAGES * gridDim.x;
+      if (next < tiles) issue(next, s);
+    }
+  }
+  if (threadIdx.x == 0) bulk_wait_all();
+}
+
 ipuc_status launch_convert(Side src, Side dst, int64_t logical_rows, int64_t logical_cols, int64_t matrices,
                            cudaStream_t stream) {
   ipuc_status st = check_side(src, "source");
@@ -393,6 +500,25 @@ ipuc_status launch_convert(Side src, Side dst, int64_t logical_rows, int64_t log
   dst.vec = (dst.ld % 8 == 0 && dst.mstride % 8 == 0) ? 1 : 0;
   const int64_t blocks = matrices * ((dst.rows + 15) / 16) * ((dst.cols + 15) / 16);
   if (blocks == 0) return IPUC_OK;
+  // Row-major -> BlockMajor{64,16} over whole 64x64 tiles (no padding): TMA path.
+  if (src.order == IPUC_ORDER_ROW_MAJOR && dst.order == IPUC_ORDER_BLOCK_MAJOR && dst.rb == 64 && dst.cb == 16 &&
+      src.rows == dst.rows && src.cols == dst.cols && logical_rows == dst.rows && logical_cols == dst.cols &&
+      src.ld == src.cols && src.mstride == src.rows * src.cols && dst.mstride == dst.rows * dst.cols &&
+      dst.rows % 64 == 0 && dst.cols % 64 == 0 && matrices < (1ll << 31)) {
+    CUtensorMap map;
+    ipuc_status ms = make_map_3d(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, src.ptr, (uint64_t)src.cols,
+                                 (uint64_t)src.rows, (uint64_t)matrices, (uint64_t)src.cols,
+                                 (uint64_t)(src.rows * src.cols), 64, 64);
+    if (ms != IPUC_OK) return ms;
+    const int32_t band_tiles = (int32_t)(dst.cols / 64), bands = (int32_t)(dst.rows / 64);
+    const int64_t tiles = matrices * bands * band_tiles;
+    const int64_t cap = (int64_t)sm_count() * 2;
+    const unsigned grid = (unsigned)(tiles < cap ? tiles : cap);
+    IPUC_CUDA(cudaFuncSetAttribute(rm_to_block_major64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BM64_SMEM));
+    rm_to_block_major64_kernel<<<grid, 128, BM64_SMEM, stream>>>(map, static_cast<uint16_t *>(dst.ptr), tiles,
+                                                                band_tiles, bands, dst.cols, device_error_word());
+    return check_launch("rm_to_block_major64_kernel");
+  }
   const bool fr = src.order == IPUC_ORDER_ROW_MAJOR, tr = dst.order == IPUC_ORDER_ROW_MAJOR;
   const int64_t lim = (int64_t)1 << 30;
   const int64_t work32 = matrices * ((dst.rows + 15) / 16) * (((dst.cols + 15) / 16 + 8 * kBlocksPerWarp - 1) / (8 * kBlocksPerWarp));

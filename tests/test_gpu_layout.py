@@ -30,6 +30,18 @@ def test_rearrange_bit_exact(target, matrices, R, Rp, C, Cp, rb, cb):
     assert np.array_equal(host_u16(out), want)
 
 
+@pytest.mark.parametrize("matrices,R,C", [(1, 64, 64), (3, 192, 320), (1, 4096, 4096), (2, 1024, 1088)])
+def test_rearrange_block_major_tma_path(matrices, R, C):
+    """Row-major -> BlockMajor{64,16} over whole 64x64 tiles takes the TMA +
+    ldmatrix.trans/stmatrix kernel (4096 x 4096: every CTA wraps its 8-stage
+    ring several times); bit-exact against storage.rs's index map."""
+    src = bits(R * 3 + C, matrices * R * C)
+    want = oracle.rearrange_f16(src, matrices, R, R, 2, C, C, 64, 16)
+    out = empty_u16(matrices * R * C)
+    ipuc.rearrange_f16(out, dev_u16(src), matrices, R, R, 2, C, C, 64, 16)
+    assert np.array_equal(host_u16(out), want)
+
+
 @pytest.mark.parametrize("order,matrices,R,Rp,C,Cp", [
     (0, 1, 64, 64, 64, 64), (0, 2, 7, 9, 30, 32), (0, 1, 100, 100, 17, 48),
     (1, 1, 64, 64, 64, 64), (1, 3, 30, 32, 20, 22), (1, 1, 128, 128, 1, 2),
