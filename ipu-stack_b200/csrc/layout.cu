@@ -394,7 +394,7 @@ ipuc_status check_side(const Side &s, const char *which) {
 // the tile.  About a quarter of an instruction per element, against one or more
 // for lane-level transposes, so the kernel runs at HBM speed.
 constexpr int BM64_TILE_BYTES = 64 * 64 * 2;  // 8 KB
-constexpr int BM64_STAGES = 8;                // input tiles in flight per CTA
+constexpr int BM64_STAGES = 6;                // input tiles in flight per CTA (3 CTAs per SM)
 constexpr int BM64_OUT = 3;                   // output tiles (bulk stores draining)
 constexpr int BM64_SMEM = (BM64_STAGES + BM64_OUT) * BM64_TILE_BYTES + 1024 + 256;
 
@@ -417,7 +417,7 @@ __device__ __forceinline__ void bulk_store(void *gdst, uint32_t ssrc, uint32_t b
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(128, 3)
     rm_to_block_major64_kernel(const __grid_constant__ CUtensorMap src_map, uint16_t *__restrict__ dst,
                                int64_t tiles, int32_t band_tiles, int32_t bands, int64_t cols, uint32_t *err) {
   extern __shared__ uint8_t smem_raw[];
@@ -512,7 +512,7 @@ ipuc_status launch_convert(Side src, Side dst, int64_t logical_rows, int64_t log
     if (ms != IPUC_OK) return ms;
     const int32_t band_tiles = (int32_t)(dst.cols / 64), bands = (int32_t)(dst.rows / 64);
     const int64_t tiles = matrices * bands * band_tiles;
-    const int64_t cap = (int64_t)sm_count() * 2;
+    const int64_t cap = (int64_t)sm_count() * 3;
     const unsigned grid = (unsigned)(tiles < cap ? tiles : cap);
     IPUC_CUDA(cudaFuncSetAttribute(rm_to_block_major64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BM64_SMEM));
     rm_to_block_major64_kernel<<<grid, 128, BM64_SMEM, stream>>>(map, static_cast<uint16_t *>(dst.ptr), tiles,
