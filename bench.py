@@ -305,6 +305,11 @@ def run_ours(args):
     peak_burst, peak_sus, hbm, peak_kind = load_peaks()
     if rank == 0:
         comps = measure_components(ipuc, torch, stream, hbm)
+    if world > 1:
+        barrier(world)
+        tp = transformer_block_tp(torch, rank, world)
+        if rank == 0:
+            comps["transformer_block_tp"] = tp
 
     # ---- CPU baseline (oracle, bounded sample, rank 0 at N=1) ----
     cpu = None
@@ -459,6 +464,38 @@ def transformer_block(ipuc, torch, stream):
            "steps": sess.plan.count("\n")}
     sess.close()
     return out
+
+
+def transformer_block_tp(torch, rank, world):
+    """Config 5 over all ranks, Megatron tensor parallel (ipuc.tp): QKV and MLP-up
+    split by columns, output and MLP-down projections by rows, one NCCL
+    all-reduce after each half.  Device time, max over ranks; TFLOP/s of the
+    whole block."""
+    from ipuc.tp import TensorParallelBlock
+    B, S, d, H, ff = 4, 2048, 4096, 32, 16384
+    blk = TensorParallelBlock(B, S, d, H, ff, rank, world)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(77)  # the same full weights and input on every rank
+    full = {n: (torch.randn(shp, generator=g, device="cuda") * 0.02).half()
+            for n, shp in [("wq", (d, d)), ("wk", (d, d)), ("wv", (d, d)), ("wo", (d, d)), ("w1", (d, ff)),
+                           ("w2", (ff, d))]}
+    blk.load(full)
+    del full
+    x = torch.randn((B * S, d), generator=g, device="cuda").half()
+    for _ in range(3):
+        blk.forward(x)
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(5):
+        blk.forward(x)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / 5, world)
+    return {"ms": round(ms, 4), "tflops": round(blk.flop / (ms * 1e-3) / 1e12, 1), "flop": blk.flop,
+            "parallelism": f"tp{world}", "collective": "2 NCCL all-reduces of 64 MiB (f16) per block"}
 
 
 # ---------------------------------------------------------------------------
