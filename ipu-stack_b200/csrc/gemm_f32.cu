@@ -297,6 +297,206 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// CTA-pair form (cluster of 2, tcgen05.mma.cta_group::2): a 256x256 tile per
+// pair, each CTA loading its own 128 rows of the A planes and 128 rows of the
+// K-major B planes, the leader issuing M256 N256 K8 MMAs.  Per CTA this halves
+// the shared-memory traffic of B (TMA fill + operand reads), which bounds the
+// single-CTA kernel.
+constexpr int P_STAGE_BYTES = 2 * A_BYTES + 2 * A_BYTES;  // A hi/lo + half of B hi/lo: 64 KB
+constexpr int P_STAGES = 3;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int PAIR_BM = 2 * BM;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+                            const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
+                            const Gemm32Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t *empty = full + P_STAGES;
+  uint64_t *acc_full = empty + P_STAGES;
+  uint64_t *acc_empty = acc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);   // the leader's arrive_expect_tx; both CTAs' bytes land on it
+      mbar_init(&empty[s], 1);  // one multicast commit per stage use
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * (EPI_THREADS / 32));  // lane 0 of every epilogue warp of both CTAs
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int chunks = (p.k_blocks + KC - 1) / KC;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
+        int mt, nt;
+        tile_coords(p, t, mt, nt);  // mt counts 256-row pair tiles
+        const int32_t arow = mt * PAIR_BM + (int32_t)rank * BM, brow = nt * BN + (int32_t)rank * (BN / 2);
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *st = smem + s * P_STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE_BYTES);
+          tma_load_3d_pair(st, &tmAh, &full[s], kb * BK, arow, 0);
+          tma_load_3d_pair(st + A_BYTES, &tmAl, &full[s], kb * BK, arow, 0);
+          tma_load_3d_pair(st + 2 * A_BYTES, &tmBh, &full[s], kb * BK, brow, 0);
+          tma_load_3d_pair(st + 3 * A_BYTES, &tmBl, &full[s], kb * BK, brow, 0);
+        }
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_PRODUCER);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*tf32*/ 2, false, false);
+      // Descriptors built once; stages and k-steps add offsets in 16-byte units.
+      const uint64_t d0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      uint32_t it = 0, g = 0;
+      bool ok = true;
+      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
+        for (int c = 0; c < chunks && ok; ++c, ++g) {
+          const uint32_t buf = g & 1u, use = g >> 1;
+          if (!mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * BN;
+          const int kb_end = min(p.k_blocks, (c + 1) * KC);
+          for (int kb = c * KC; kb < kb_end; ++kb, ++it) {
+            const int s = it % P_STAGES;
+            const uint32_t ph = (it / P_STAGES) & 1u;
+            if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t dah = d0 + (uint64_t)(s * (P_STAGE_BYTES >> 4));
+            const uint64_t dal = dah + (uint64_t)(A_BYTES >> 4);
+            const uint64_t dbh = dah + (uint64_t)((2 * A_BYTES) >> 4);
+            const uint64_t dbl = dah + (uint64_t)((3 * A_BYTES) >> 4);
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k) {
+              const uint64_t o = (uint64_t)((k * 32) >> 4);
+              // Small terms first, then the dominant hi.hi product.
+              mma_tf32_ss_pair(d_tmem, dal + o, dbh + o, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
+              mma_tf32_ss_pair(d_tmem, dah + o, dbl + o, idesc, 1u);
+              mma_tf32_ss_pair(d_tmem, dah + o, dbh + o, idesc, 1u);
+            }
+            mma_commit_pair(&empty[s], 0x3);
+          }
+          if (!ok) break;
+          mma_commit_pair(&acc_full[buf], 0x3);
+        }
+      }
+      if (!ok) {
+        record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_MMA);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp >= 2) {
+    // 8 epilogue warps per CTA, as in the single-CTA kernel: warp w owns TMEM
+    // lanes of quarter w%4 (this CTA's 128 rows) and the column half (w-2)/4.
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const bool accumulate = (p.flags & IPUC_GEMM_ACCUMULATE) != 0;
+    const bool vec_ok = (p.ldc % 4 == 0);
+    uint32_t g = 0;
+    bool ok = true;
+    for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
+      float acc[BN / 2];
+#pragma unroll
+      for (int i = 0; i < BN / 2; ++i) acc[i] = 0.0f;
+      for (int c = 0; c < chunks; ++c, ++g) {
+        const uint32_t buf = g & 1u, use = g >> 1;
+        if (!mbar_wait_bounded(&acc_full[buf], use & 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int ch = 0; ch < BN / 64; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + buf * BN + half * (BN / 2) + ch * 32 + ((uint32_t)(quarter * 32) << 16), r);
+          tmem_wait_ld(r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[ch * 32 + i] += __uint_as_float(r[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_leader(&acc_empty[buf]);
+      }
+      if (!ok) break;
+      int mt, nt;
+      tile_coords(p, t, mt, nt);
+      const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
+      const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
+      if (row < p.m) {
+        float *cp = p.c + row * p.ldc + col_base;
+        if (vec_ok && col_base + BN / 2 <= p.n) {
+          float4 *c4 = reinterpret_cast<float4 *>(cp);
+#pragma unroll
+          for (int j = 0; j < BN / 8; ++j) {
+            float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+            if (accumulate) {
+              const float4 o = c4[j];
+              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+            }
+            c4[j] = v;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 2; ++j) {
+            if (col_base + j < p.n) {
+              float x = acc[j];
+              if (accumulate) x += cp[j];
+              cp[j] = x;
+            }
+          }
+        }
+      }
+    }
+    if (!ok) {
+      record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_EPILOGUE);
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 inline uint64_t round256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
 }  // namespace
@@ -359,13 +559,29 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
   p.c = c;
   p.m = m; p.n = n; p.k = k;
   p.ldc = ldc;
-  p.tiles_m = (int32_t)((m + BM - 1) / BM);
   p.tiles_n = (int32_t)((n + BN - 1) / BN);
   p.k_blocks = (int32_t)((k + BK - 1) / BK);
-  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
   p.flags = flags;
   p.err = device_error_word();
-  const int grid = (int)(p.num_tiles < sm_count() ? p.num_tiles : sm_count());
+  const int sms = sm_count();
+  const int64_t pair_tiles = ((m + PAIR_BM - 1) / PAIR_BM) * (int64_t)p.tiles_n;
+  if (m > BM && sms >= 2 && pair_tiles >= sms / 2) {
+    // CTA pairs (at least one full wave of 256x256 tiles; below that the
+    // single-CTA kernel spreads the work over more SMs): A boxes of 128 rows
+    // per CTA, B boxes of 128 rows (half of BN).
+    CUtensorMap pbh, pbl;
+    if ((st = make_map_3d(&pbh, f32, 4, bh, k, n, 1, k, 0, BK, BN / 2)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&pbl, f32, 4, bl, k, n, 1, k, 0, BK, BN / 2)) != IPUC_OK) return st;
+    p.tiles_m = (int32_t)((m + PAIR_BM - 1) / PAIR_BM);
+    p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
+    const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    IPUC_CUDA(cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+    gemm_tf32x3_pair_kernel<<<(unsigned)(2 * pairs), NUM_THREADS, P_SMEM_BYTES, stream>>>(tah, tal, pbh, pbl, p);
+    return check_launch("gemm_tf32x3_pair_kernel");
+  }
+  p.tiles_m = (int32_t)((m + BM - 1) / BM);
+  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
+  const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
   IPUC_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tah, tal, tbh, tbl, p);
   return check_launch("gemm_tf32x3_kernel");

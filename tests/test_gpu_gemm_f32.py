@@ -48,6 +48,21 @@ def test_gemm_f32_accumulate():
     assert rel_l2(got, ref) <= 1e-5
 
 
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_f32_pair_path_ragged(bt):
+    """At least a wave of 256x256 tiles takes the CTA-pair kernel: ragged rows
+    (2200 = 8.6 pair tiles), a column tail (4104 = 16 * 256 + 8) and a K tail
+    (200 = 6.25 blocks of 32)."""
+    got, ref, _, _ = run(2200, 4104, 200, ipuc.GEMM_B_TRANSPOSED if bt else 0, seed=31)
+    assert rel_l2(got, ref) <= 1e-5
+
+
+def test_gemm_f32_pair_path_accumulate():
+    c0 = seeded_uniform(12, (2048, 2560))
+    got, ref, _, _ = run(2048, 2560, 1000, ipuc.GEMM_ACCUMULATE, c0=c0, seed=13)
+    assert rel_l2(got, ref) <= 1e-5
+
+
 def test_gemm_f32_workspace_checked():
     a = torch.zeros((64, 64), device="cuda")
     small = torch.empty(16, dtype=torch.uint8, device="cuda")
