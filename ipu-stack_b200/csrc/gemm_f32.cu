@@ -64,28 +64,62 @@ __global__ void __launch_bounds__(256) split_tf32_kernel(const float *__restrict
 }
 
 // hi/lo planes of B^T: B is row-major [rows x cols] (ld); the planes are dense
-// [cols x rows], so the MMA reads B K-major.  32x32 tiles through shared memory
-// keep both the reads and the writes coalesced.
+// [cols x rows], so the MMA reads B K-major.  64x64 tiles through shared memory,
+// 16-byte loads and stores (each thread moves 16 elements each way) so that
+// enough bytes are in flight per SM to run near HBM bandwidth; the padded tile
+// row (65 floats) keeps the column reads conflict-free.  Vector accesses need
+// rows, cols and ld to be multiples of 4 (the gemm_f32 entry requires that);
+// ragged 64x64 tiles fall back to scalar accesses.
 __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float *__restrict__ src, int64_t rows,
                                                                    int64_t cols, int64_t ld, float *__restrict__ hi,
                                                                    float *__restrict__ lo) {
-  __shared__ float tile[32][33];
-  const int64_t tr = (rows + 31) / 32, tc = (cols + 31) / 32;
+  __shared__ float tile[64][65];
+  const int64_t tr = (rows + 63) / 64, tc = (cols + 63) / 64;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads, 4 consecutive elements each
   for (int64_t t = blockIdx.x; t < tr * tc; t += gridDim.x) {
-    const int64_t r0 = (t / tc) * 32, c0 = (t % tc) * 32;
+    const int64_t r0 = (t / tc) * 64, c0 = (t % tc) * 64;
+    const bool full = r0 + 64 <= rows && c0 + 64 <= cols;
     __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += 8) {
-      const int64_t r = r0 + i, c = c0 + threadIdx.x;
-      tile[i][threadIdx.x] = (r < rows && c < cols) ? src[r * ld + c] : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = ty + 16 * i, cc = tx * 4;
+      const int64_t r = r0 + rr, c = c0 + cc;
+      float4 v;
+      if (full) {
+        v = *reinterpret_cast<const float4 *>(src + r * ld + c);
+      } else {
+        v.x = (r < rows && c < cols) ? src[r * ld + c] : 0.0f;
+        v.y = (r < rows && c + 1 < cols) ? src[r * ld + c + 1] : 0.0f;
+        v.z = (r < rows && c + 2 < cols) ? src[r * ld + c + 2] : 0.0f;
+        v.w = (r < rows && c + 3 < cols) ? src[r * ld + c + 3] : 0.0f;
+      }
+      tile[rr][cc] = v.x;
+      tile[rr][cc + 1] = v.y;
+      tile[rr][cc + 2] = v.z;
+      tile[rr][cc + 3] = v.w;
     }
     __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += 8) {
-      const int64_t c = c0 + i, r = r0 + threadIdx.x;  // output row c, column r
-      if (c < cols && r < rows) {
-        const float x = tile[threadIdx.x][i];
-        const float h = to_tf32(x);
-        hi[c * rows + r] = h;
-        lo[c * rows + r] = to_tf32(x - h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int oc = ty + 16 * i, orr = tx * 4;  // output row = source column c0 + oc
+      const int64_t c = c0 + oc, r = r0 + orr;
+      float x[4], h[4], l[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[e] = tile[orr + e][oc];
+        h[e] = to_tf32(x[e]);
+        l[e] = to_tf32(x[e] - h[e]);
+      }
+      if (full) {
+        *reinterpret_cast<float4 *>(hi + c * rows + r) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(lo + c * rows + r) = make_float4(l[0], l[1], l[2], l[3]);
+      } else if (c < cols) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (r + e < rows) {
+            hi[c * rows + r + e] = h[e];
+            lo[c * rows + r + e] = l[e];
+          }
       }
     }
   }
@@ -541,9 +575,9 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
   if (bt) {
     split_tf32_kernel<<<grid_of(brows * bcols), 256, 0, stream>>>(b, brows, bcols, ldb, bh, bl);
   } else {
-    const int64_t tiles = ((k + 31) / 32) * ((n + 31) / 32);
+    const int64_t tiles = ((k + 63) / 64) * ((n + 63) / 64);
     const unsigned g = (unsigned)(tiles < cap ? tiles : cap);
-    split_tf32_transpose_kernel<<<g, dim3(32, 8), 0, stream>>>(b, k, n, ldb, bh, bl);
+    split_tf32_transpose_kernel<<<g, 256, 0, stream>>>(b, k, n, ldb, bh, bl);
   }
   ipuc_status st = check_launch("split_tf32_kernel");
   if (st != IPUC_OK) return st;
