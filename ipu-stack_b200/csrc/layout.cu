@@ -9,11 +9,14 @@
 // Every packed order of crates/ipu-codegen/src/storage.rs stores each 16x16
 // micro-block of a matrix as 256 contiguous elements, with an order-specific
 // permutation inside the block (derivation per order in block_base /
-// block_offset below).  The kernel therefore moves one micro-block per warp:
-// each lane reads one 16-byte chunk of the source block, the warp transposes
-// through a 16x16 shared-memory tile, and each lane writes one 16-byte chunk
-// of the destination block.  Global traffic is one read and one write of
-// each byte in full 32-byte sectors (HBM-bound, no tensor cores).
+// block_offset below).  The general kernel therefore moves one micro-block per
+// warp: each lane reads one 16-byte chunk of the source block, the warp
+// transposes through a 16x16 shared-memory tile, and each lane writes one
+// 16-byte chunk of the destination block.  Global traffic is one read and one
+// write of each byte in full 32-byte sectors (HBM-bound, no tensor cores).
+// Row-major -> BlockMajor{64,16} over whole 64x64 tiles (the config-5 weight
+// layout) has a dedicated TMA + ldmatrix/stmatrix kernel
+// (rm_to_block_major64_kernel) that moves whole contiguous 8 KB tiles.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
