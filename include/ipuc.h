@@ -184,6 +184,19 @@ ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_precision, co
                                      int64_t query_rows, int64_t key_rows, int64_t head_dim,
                                      float scale, ipuc_stream stream);
 
+/* The same attention with SplitHeads and its inverse folded into the memory
+ * access (graph.rs:336-343; the copy-free strided form):
+ *   Q [batch][query_rows][heads * head_dim], K and V [batch][key_rows][heads *
+ *   head_dim], out [batch][query_rows][heads * head_dim]; stream (b, h) reads
+ *   columns [h * head_dim, (h + 1) * head_dim) of its batch entry's rows.
+ * Equals merge_heads(attention(split_heads(q), split_heads(k), split_heads(v)))
+ * with no split or merge copies.  Same limits as ipuc_flash_attention_f16;
+ * heads * head_dim is the row length. */
+ipuc_status ipuc_flash_attention_heads_f16(void *out, ipuc_precision out_precision, const void *q,
+                                           const void *k, const void *v, int64_t batch, int64_t heads,
+                                           int64_t query_rows, int64_t key_rows, int64_t head_dim,
+                                           float scale, ipuc_stream stream);
+
 /* AttentionSoftmax (device/attention_softmax_f16.cpp:63-139, asm variant
  * device/attention_stages_f16.S:54-695): one key block per call.
  *   scores  f16 panels [key_block_columns/16][query_rows][16]

@@ -50,6 +50,7 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   int32_t out_f32;
   int32_t key_tiles;
+  int32_t heads;      // streams per batch entry: Q/K/V/O are [batch][rows][heads * d] (1: [streams][rows][d])
   int32_t q_units;    // query units per stream: 512-row (pair, split) or 256-row blocks
   int64_t unit_base;  // first unit of this launch (split: first 256-row half-unit)
   uint32_t *err;
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int K_HALF = K_BYTES / 2;                             // one 64-column head-dim half
   constexpr int V_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA V tile (64 or 128 D columns)
   constexpr int TX_MULT = kPair ? 2 : 1;                          // leader counts both CTAs' bytes
+  const int32_t s_head = (int32_t)(stream % p.heads), s_batch = (int32_t)(stream / p.heads);
   // Key tiles [j_begin, j_begin + n_tiles) of the stream; loop counters below
   // are local (they set stage and phase), key coordinates add j_begin.
   const int split_half = (p.key_tiles + 1) / 2;
@@ -158,8 +160,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       bool ok = true;
       auto load = [&](void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x, int32_t y) {
-        if (kPair) tma_load_3d_pair(dst, map, bar, x, y, (int32_t)stream);
-        else tma_load_3d(dst, map, bar, x, y, (int32_t)stream);
+        // 4-D maps (head_dim, heads, rows, batch): a stream is (batch, head).
+        if (kPair) tma_load_4d_pair(dst, map, bar, x, s_head, y, s_batch);
+        else tma_load_4d(dst, map, bar, x, s_head, y, s_batch);
       };
       if (leader) mbar_arrive_expect_tx(q_full, TX_MULT * 2 * TILE_BYTES);
       for (int t = 0; t < 2; ++t)
@@ -390,7 +393,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int64_t grow = (int64_t)q0 + t * TQ + row;
       const bool row_ok = grow < p.sq;
-      const int64_t base = (stream * p.sq + grow) * p.d;
+      const int64_t base = ((s_batch * p.sq + grow) * p.heads + s_head) * p.d;
       // Split merge area in CTA 0: its Q/K/V tiles, dead once its MMAs are
       // complete.  Rows are padded to RECV_LD floats so that one warp's
       // float4 reads of 32 rows spread over all banks.
@@ -498,11 +501,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 using namespace ipuc;
 
-extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_precision, const void *q, const void *k,
-                                                const void *v, int64_t matrices, int64_t query_rows, int64_t key_rows,
-                                                int64_t head_dim, float scale, ipuc_stream stream) {
+namespace ipuc {
+namespace {
+// Streams = batch * heads; Q [batch][query_rows][heads * head_dim], K and V
+// [batch][key_rows][heads * head_dim], out [batch][query_rows][heads * head_dim]
+// (heads = 1: [streams][rows][head_dim]).
+ipuc_status attention_launch(void *out, ipuc_precision out_precision, const void *q, const void *k, const void *v,
+                             int64_t batch, int64_t heads, int64_t query_rows, int64_t key_rows, int64_t head_dim,
+                             float scale, cudaStream_t stream) {
   IPUC_CHECK_ARG(out_precision == IPUC_F16 || out_precision == IPUC_F32, "flash_attention: bad output precision");
-  IPUC_CHECK_ARG(matrices >= 0 && query_rows >= 0 && key_rows >= 0, "flash_attention: negative extent");
+  IPUC_CHECK_ARG(batch >= 0 && heads >= 1 && query_rows >= 0 && key_rows >= 0, "flash_attention: negative extent");
+  const int64_t matrices = batch * heads;
   if (matrices == 0 || query_rows == 0) return IPUC_OK;
   IPUC_CHECK_ARG(key_rows > 0, "flash_attention: key rows must be positive");
   IPUC_CHECK_ARG(head_dim > 0 && head_dim % 8 == 0, "flash_attention: head_dim must be a positive multiple of 8");
@@ -510,19 +519,22 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
   IPUC_CHECK_ARG(out && q && k && v, "flash_attention: null pointer");
   IPUC_CHECK_ALIGN(aligned(out, 16) && aligned(q, 16) && aligned(k, 16) && aligned(v, 16),
                    "flash_attention: pointers must be 16-byte aligned");
-  IPUC_CHECK_ARG(matrices < 65536 && query_rows < (1ll << 31) && key_rows < (1ll << 31),
+  IPUC_CHECK_ARG(matrices < (1ll << 24) && heads < (1ll << 16) && query_rows < (1ll << 31) && key_rows < (1ll << 31),
                  "flash_attention: extent too large");
   // CTA pairs when every pair gets a full 512-row query block.
   const bool pair = query_rows >= 4 * TQ;
   CUtensorMap tq, tk, tv, tk_full;
-  ipuc_status st = make_map_3d(&tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q, head_dim, query_rows, matrices, head_dim,
-                               query_rows * head_dim, 64, TQ);
+  // 4-D maps (head_dim, heads, rows, batch): one stream's rows sit head_dim
+  // apart within a row of heads * head_dim, so split-heads costs no copy.
+  const int64_t ld = heads * head_dim;
+  const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  ipuc_status st = make_map_4d_rows(&tq, f16, 2, q, head_dim, heads, query_rows, batch, head_dim, ld,
+                                    query_rows * ld, 64, TQ);
   if (st != IPUC_OK) return st;
-  st = make_map_3d(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, k, head_dim, key_rows, matrices, head_dim,
-                   key_rows * head_dim, 64, pair ? TK / 2 : TK);
+  st = make_map_4d_rows(&tk, f16, 2, k, head_dim, heads, key_rows, batch, head_dim, ld, key_rows * ld, 64,
+                        pair ? TK / 2 : TK);
   if (st != IPUC_OK) return st;
-  st = make_map_3d(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, v, head_dim, key_rows, matrices, head_dim,
-                   key_rows * head_dim, 64, TK);
+  st = make_map_4d_rows(&tv, f16, 2, v, head_dim, heads, key_rows, batch, head_dim, ld, key_rows * ld, 64, TK);
   if (st != IPUC_OK) return st;
   AttnParams p;
   p.out = out;
@@ -534,6 +546,7 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
   p.scale_log2 = s * 1.4426950408889634f;
   p.out_f32 = out_precision == IPUC_F32;
   p.key_tiles = (int32_t)((key_rows + TK - 1) / TK);
+  p.heads = (int32_t)heads;
   p.unit_base = 0;
   p.err = device_error_word();
   auto launch = [&](auto kernel, int64_t ctas, bool cluster, const CUtensorMap &kmap) -> ipuc_status {
@@ -570,10 +583,26 @@ extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_pr
     if (st != IPUC_OK) return st;
   }
   if (!split) return IPUC_OK;
-  st = make_map_3d(&tk_full, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, k, head_dim, key_rows, matrices, head_dim,
-                   key_rows * head_dim, 64, TK);
+  st = make_map_4d_rows(&tk_full, f16, 2, k, head_dim, heads, key_rows, batch, head_dim, ld, key_rows * ld, 64, TK);
   if (st != IPUC_OK) return st;
   p.unit_base = 2 * full;  // 256-row half-units
   return launch(flash_attention_kernel<false, true>, 4 * tail, true, tk_full);
+}
+}  // namespace
+}  // namespace ipuc
+
+extern "C" ipuc_status ipuc_flash_attention_f16(void *out, ipuc_precision out_precision, const void *q, const void *k,
+                                                const void *v, int64_t matrices, int64_t query_rows, int64_t key_rows,
+                                                int64_t head_dim, float scale, ipuc_stream stream) {
+  return ipuc::attention_launch(out, out_precision, q, k, v, matrices, 1, query_rows, key_rows, head_dim, scale,
+                                stream);
+}
+
+extern "C" ipuc_status ipuc_flash_attention_heads_f16(void *out, ipuc_precision out_precision, const void *q,
+                                                      const void *k, const void *v, int64_t batch, int64_t heads,
+                                                      int64_t query_rows, int64_t key_rows, int64_t head_dim,
+                                                      float scale, ipuc_stream stream) {
+  return ipuc::attention_launch(out, out_precision, q, k, v, batch, heads, query_rows, key_rows, head_dim, scale,
+                                stream);
 }
 

@@ -50,6 +50,7 @@ SIGNATURES = {
     "ipuc_add_f16": (_i32, [_vp, _vp, _vp, _u64, _u64, _u64, _vp]),
     "ipuc_cast": (_i32, [_vp, _i32, _vp, _i32, _u64, _vp]),
     "ipuc_flash_attention_f16": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _vp]),
+    "ipuc_flash_attention_heads_f16": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _vp]),
     "ipuc_attention_softmax_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ipuc_attention_merge_f16": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "ipuc_rearrange_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _i64, _vp]),
@@ -191,6 +192,13 @@ def flash_attention_f16(out, q, k, v, matrices, query_rows, key_rows, head_dim, 
                         stream=None):
     call("ipuc_flash_attention_f16", _ptr(out), out_precision, _ptr(q), _ptr(k), _ptr(v), matrices, query_rows,
          key_rows, head_dim, scale, _stream(stream))
+
+
+def flash_attention_heads_f16(out, q, k, v, batch, heads, query_rows, key_rows, head_dim, out_precision=F16,
+                              scale=0.0, stream=None):
+    """Attention on [batch, rows, heads * head_dim] tensors (split/merge heads folded in)."""
+    call("ipuc_flash_attention_heads_f16", _ptr(out), out_precision, _ptr(q), _ptr(k), _ptr(v), batch, heads,
+         query_rows, key_rows, head_dim, scale, _stream(stream))
 
 
 def attention_softmax_f16(weights, scores, query_rows, key_rows, key_block_columns, head_dimension, stream=None):

@@ -12,7 +12,7 @@ import torch
 import ipuc
 import oracle
 from conftest import f16_close
-from gpu_util import dev_u16, f16_of, host_f32, host_u16
+from gpu_util import dev_u16, empty_u16, f16_of, host_f32, host_u16
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
@@ -105,6 +105,27 @@ def test_attention_split_merge_rescale():
     got = run(q, k, v, out_f32=True)
     ref = oracle.attention(f16_of(q), f16_of(k), f16_of(v))
     ok, msg = f16_close(got, ref)
+    assert ok, msg
+
+
+@pytest.mark.parametrize("B,H,S,D,out_f32", [(2, 3, 300, 64, False), (1, 4, 1024, 128, False), (2, 2, 513, 128, True)])
+def test_attention_heads_layout(B, H, S, D, out_f32):
+    """ipuc_flash_attention_heads_f16 on [batch, rows, heads*head_dim] tensors
+    equals merge_heads(attention(split_heads(.))) (graph.rs:336-343)."""
+    rng = np.random.default_rng(B * 100 + H * 10 + S)
+    q, k, v = (oracle.f16_bits(rng.standard_normal((B, S, H * D)).astype(np.float32)) for _ in range(3))
+    split = lambda x: f16_of(x).reshape(B, S, H, D).transpose(0, 2, 1, 3).reshape(B * H, S, D)
+    ref = oracle.attention(split(q), split(k), split(v), threads=8)
+    ref = ref.reshape(B, H, S, D).transpose(0, 2, 1, 3).reshape(B, S, H * D)
+    if out_f32:
+        out = torch.empty(B * S * H * D, dtype=torch.float32, device="cuda")
+    else:
+        out = empty_u16(B * S * H * D)
+        ref = oracle.quantize_f16(ref)
+    ipuc.flash_attention_heads_f16(out, dev_u16(q), dev_u16(k), dev_u16(v), B, H, S, S, D,
+                                   out_precision=ipuc.F32 if out_f32 else ipuc.F16)
+    got = host_f32(out) if out_f32 else f16_of(host_u16(out))
+    ok, msg = f16_close(got.reshape(B, S, H * D), ref)
     assert ok, msg
 
 
