@@ -102,7 +102,7 @@ struct ipug_graph {
 
 namespace {
 
-enum class StepKind { Gemm, Gelu, Add, SplitHeads, MergeHeads, Attention, Copy };
+enum class StepKind { Gemm, Gelu, Add, SplitHeads, MergeHeads, Attention, AttentionHeads, Copy };
 
 struct Step {
   StepKind kind;
@@ -169,6 +169,31 @@ ipuc_status lower(const ipug_graph &g, ipug_session &s) {
         fused_gemm[c] = (int32_t)i;
       }
     }
+  }
+
+  // SplitHeads(q), SplitHeads(k), SplitHeads(v) -> FlashAttention -> MergeHeads,
+  // with every intermediate used once and not an output, lowers to one
+  // attention call on the unsplit [b, rows, heads * c] values (4-D tensor maps
+  // stand in for the split and merge copies).  fused_attention[merge op] =
+  // attention op; the split and attention ops emit no step.
+  std::vector<int32_t> fused_attention(g.ops.size(), -1);
+  auto single_use = [&](int32_t v) { return !is_output[v] && consumers[v].size() == 1; };
+  for (size_t i = 0; i < g.ops.size(); ++i) {
+    const Op &at = g.ops[i];
+    if (at.kind != OpKind::FlashAttention || at.causal || !single_use(at.result)) continue;
+    const Op &mg = g.ops[consumers[at.result][0]];
+    if (mg.kind != OpKind::MergeHeads) continue;
+    bool ok = true;
+    for (int32_t in : at.inputs) {
+      const Value &val = g.values[in];
+      if (val.kind != 2 || !single_use(in)) { ok = false; break; }
+      const Op &sp = g.ops[val.producer];
+      ok = ok && sp.kind == OpKind::SplitHeads && sp.heads == mg.heads && g.values[sp.inputs[0]].shape.size() == 3;
+    }
+    if (!ok) continue;
+    fused_attention[consumers[at.result][0]] = (int32_t)i;
+    fused_into_next[i] = true;
+    for (int32_t in : at.inputs) fused_into_next[g.values[in].producer] = true;
   }
 
   auto gemm_step = [&](const Op &op, Step &st) -> ipuc_status {
@@ -285,6 +310,34 @@ ipuc_status lower(const ipug_graph &g, ipug_session &s) {
         break;
       }
       case OpKind::MergeHeads: {
+        if (fused_attention[i] >= 0) {
+          // Attention on the unsplit projections, written in merged layout.
+          const Op &at = g.ops[fused_attention[i]];
+          const Op &sq = g.ops[g.values[at.inputs[0]].producer], &sk = g.ops[g.values[at.inputs[1]].producer],
+                   &sv = g.ops[g.values[at.inputs[2]].producer];
+          const auto &qx = g.values[sq.inputs[0]].shape, &kx = g.values[sk.inputs[0]].shape,
+                     &vx = g.values[sv.inputs[0]].shape;
+          if (qx[0] != kx[0] || kx != vx || qx[2] != kx[2]) {
+            rc = ipuc::fail(IPUC_ERR_UNSUPPORTED, "lowering: attention needs equal batch and width for q, k and v");
+            break;
+          }
+          st.kind = StepKind::AttentionHeads;
+          st.op_ids = {g.values[at.inputs[0]].producer, g.values[at.inputs[1]].producer,
+                       g.values[at.inputs[2]].producer, fused_attention[i], (int32_t)i};
+          st.in0 = sq.inputs[0];
+          st.in1 = sk.inputs[0];
+          st.in2 = sv.inputs[0];
+          st.b = qx[0];
+          st.heads = op.heads;
+          st.sq = qx[1];
+          st.sk = kx[1];
+          st.d = qx[2] / op.heads;
+          st.streams = st.b * st.heads;
+          st.scale = at.scale;
+          st.flop = 4.0 * st.streams * st.sq * st.sk * st.d;
+          st.label = "flash_attention_heads_f16";
+          break;
+        }
         st.kind = StepKind::MergeHeads;
         const auto &x = g.values[op.inputs[0]].shape;
         st.in0 = op.inputs[0];
@@ -332,7 +385,7 @@ ipuc_status lower(const ipug_graph &g, ipug_session &s) {
     plan << " out=v" << st.out << shape_str(g.values[st.out].shape) << "\n";
   }
   s.plan = plan.str();
-  // Buffers: every value except Gemm results fused into their consumer.
+  // Buffers: every value except the results of ops fused into a consumer.
   s.buffers.assign(nv, nullptr);
   for (size_t v = 0; v < nv; ++v) {
     const Value &val = g.values[v];
@@ -365,6 +418,9 @@ ipuc_status run_step(ipug_session &s, const Step &st, cudaStream_t stream) {
     case StepKind::Attention:
       return ipuc_flash_attention_f16(P(st.out), IPUC_F16, P(st.in0), P(st.in1), P(st.in2), st.streams, st.sq, st.sk,
                                       st.d, st.scale, stream);
+    case StepKind::AttentionHeads:
+      return ipuc_flash_attention_heads_f16(P(st.out), IPUC_F16, P(st.in0), P(st.in1), P(st.in2), st.b, st.heads,
+                                            st.sq, st.sk, st.d, st.scale, stream);
     case StepKind::Copy: {
       const cudaError_t e = cudaMemcpyAsync(P(st.out), P(st.in0), st.count * 2, cudaMemcpyDeviceToDevice, stream);
       if (e != cudaSuccess) return ipuc::fail(IPUC_ERR_CUDA, std::string("session copy: ") + cudaGetErrorString(e));

@@ -10,8 +10,8 @@ The residual adds are folded into rank 0's partial sum (its GEMM accumulates
 onto the residual), so each all-reduce yields the residual sum directly.
 
 Compute is the library's kernels (ipuc_gemm_f16 with the fused GELU/accumulate
-epilogues, ipuc_split_heads_f16 / ipuc_flash_attention_f16 /
-ipuc_merge_heads_f16); the all-reduce is NCCL through torch.distributed.
+epilogues, and ipuc_flash_attention_heads_f16 reading the local heads straight
+out of the QKV projections); the all-reduce is NCCL through torch.distributed.
 The shard planning (`plan`) is plain host logic, tested on CPU.
 """
 
@@ -65,8 +65,7 @@ class TensorParallelBlock:
         self.wq, self.wk, self.wv = e(d, self.dl), e(d, self.dl), e(d, self.dl)
         self.wo, self.w1, self.w2 = e(self.dl, d), e(d, self.fl), e(self.fl, d)
         self.qf, self.kf, self.vf = e(T, self.dl), e(T, self.dl), e(T, self.dl)
-        self.q, self.k, self.v = (e(batch * self.hl, seq, self.dh) for _ in range(3))
-        self.att, self.a = e(batch * self.hl, seq, self.dh), e(T, self.dl)
+        self.a = e(T, self.dl)
         self.h, self.u, self.y = e(T, d), e(T, self.fl), e(T, d)
 
     def load(self, weights: dict) -> None:
@@ -97,11 +96,9 @@ class TensorParallelBlock:
         T, d = self.B * self.S, self.d
         for w, out in ((self.wq, self.qf), (self.wk, self.kf), (self.wv, self.vf)):
             self._gemm(out, x, w, T, self.dl, d, 0, s)
-        for flat, heads in ((self.qf, self.q), (self.kf, self.k), (self.vf, self.v)):
-            call("ipuc_split_heads_f16", heads.data_ptr(), flat.data_ptr(), self.B, self.S, self.hl, self.dh, s)
-        call("ipuc_flash_attention_f16", self.att.data_ptr(), F16, self.q.data_ptr(), self.k.data_ptr(),
-             self.v.data_ptr(), self.B * self.hl, self.S, self.S, self.dh, 0.0, s)
-        call("ipuc_merge_heads_f16", self.a.data_ptr(), self.att.data_ptr(), self.B, self.S, self.hl, self.dh, s)
+        # Local heads read in place from [B, S, hl * dh] and written merged.
+        call("ipuc_flash_attention_heads_f16", self.a.data_ptr(), F16, self.qf.data_ptr(), self.kf.data_ptr(),
+             self.vf.data_ptr(), self.B, self.hl, self.S, self.S, self.dh, 0.0, s)
         # h = x + sum over ranks of a_r Wo_r (rank 0 accumulates onto x).
         if self.shard.adds_residual:
             self.h.copy_(x)

@@ -64,13 +64,35 @@ def test_transformer_block_small():
     s = run_graph(g, inputs)
     plan = s.plan
     assert plan.count("gemm_f16+add") == 2 and plan.count("gemm_f16+gelu") == 1
-    assert "flash_attention_f16" in plan and "merge_heads_f16" in plan
+    # split-heads -> attention -> merge-heads lowers to one attention call on the
+    # unsplit projections (no split or merge copies)
+    assert "flash_attention_heads_f16" in plan and "split_heads_f16" not in plan and "merge_heads_f16" not in plan
     ref = oracle.evaluate(g, inputs)[out]
     ok, msg = f16_close(s.read(out).astype(np.float32), ref)
     assert ok, msg
     prof = s.profile()
     assert len(prof["steps"]) == plan.count("\n") and prof["total_ms"] > 0
     assert any("tflops" in st for st in prof["steps"])
+
+
+def test_attention_without_merge_keeps_split_heads():
+    """An attention result that is itself a graph output is not fused with its
+    SplitHeads producers: the plan keeps the split copies and plain attention."""
+    B, S, d, H = 2, 192, 256, 2
+    g = ComputeGraph()
+    x = g.host_input("x", [B, S, d])
+    ws = {n: g.parameter(n, [d, d]) for n in ("wq", "wk", "wv")}
+    q, k, v = (g.split_heads(g.gemm(x, ws[n]), H) for n in ("wq", "wk", "wv"))
+    a = g.flash_attention(q, k, v)
+    g.set_outputs([a])
+    rng = np.random.default_rng(9)
+    inputs = {x: rng.standard_normal((B, S, d)).astype(np.float32)}
+    for n, val in ws.items():
+        inputs[val] = (rng.standard_normal((d, d)) * 0.05).astype(np.float32)
+    s = run_graph(g, inputs)
+    assert s.plan.count("split_heads_f16") == 3 and "flash_attention_f16" in s.plan
+    ok, msg = f16_close(s.read(a).astype(np.float32), oracle.evaluate(g, inputs)[a])
+    assert ok, msg
 
 
 def test_bias_broadcast_add_and_unfused_gemm():
