@@ -385,6 +385,68 @@ ipuc_status check_side(const Side &s, const char *which) {
   return fail(IPUC_ERR_INVALID_ARGUMENT, w + ": unknown element order");
 }
 
+// ---- AMP-Output -> row-major (unpack_amp_f16.cpp:40-81, source order 0) -------------
+// AMP-Output keeps 16-column panels with rows contiguous (storage.rs:330-340); inside
+// a row's 16 elements the 2-element pairs are permuted (logical pair lp sits at
+// physical pair (lp % 4) * 2 + lp / 4).  A CTA moves a tile of 32 rows x 16 panels
+// through shared memory so that both sides stay contiguous: each panel's 32 row
+// segments (1 KB) are read in order, then each row's 16 segments (512 B) are
+// written in order, the pair permutation applied in registers on the way out.
+// Elements outside the logical extent are written as 0.
+constexpr int UNP_ROWS = 32, UNP_PANELS = 16, UNP_PITCH = UNP_PANELS * 2 + 1;  // uint4 per tile row (+1 pad)
+
+__global__ void __launch_bounds__(256) unpack_amp_output_kernel(const uint16_t *__restrict__ src,
+                                                                uint16_t *__restrict__ dst, int64_t matrices,
+                                                                int64_t rows, int64_t cols, int64_t logical_rows,
+                                                                int64_t logical_cols) {
+  __shared__ uint4 tile[UNP_ROWS * UNP_PITCH];
+  const int64_t panels = cols / 16, per_matrix = rows * cols;
+  const int64_t row_tiles = (rows + UNP_ROWS - 1) / UNP_ROWS, panel_tiles = (panels + UNP_PANELS - 1) / UNP_PANELS;
+  const int64_t tiles = matrices * row_tiles * panel_tiles;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t pt = t % panel_tiles, rest = t / panel_tiles;
+    const int64_t rt = rest % row_tiles, m = rest / row_tiles;
+    const int64_t r0 = rt * UNP_ROWS, p0 = pt * UNP_PANELS;
+    const uint4 *s4 = reinterpret_cast<const uint4 *>(src + m * per_matrix);
+    __syncthreads();  // the previous tile's reads of `tile` are done
+    // Load: chunk q = (panel, row, half) with row and half fastest: a panel's rows are contiguous.
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int q = threadIdx.x + 256 * j;
+      const int pl = q >> 6, r = (q >> 1) & 31, hf = q & 1;
+      if (p0 + pl < panels && r0 + r < rows)
+        tile[r * UNP_PITCH + pl * 2 + hf] = s4[((p0 + pl) * rows + r0 + r) * 2 + hf];
+    }
+    __syncthreads();
+    // Store: segment s = (row, panel) with panel fastest: a row's segments are contiguous.
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int sg = threadIdx.x + 256 * j;
+      const int r = sg >> 4, pl = sg & 15;
+      const int64_t row = r0 + r, p = p0 + pl;
+      if (p >= panels || row >= rows) continue;
+      const uint4 a = tile[r * UNP_PITCH + pl * 2], b = tile[r * UNP_PITCH + pl * 2 + 1];
+      // logical pairs 0..7 <- physical pairs 0, 2, 4, 6, 1, 3, 5, 7
+      uint32_t w[8] = {a.x, a.z, b.x, b.z, a.y, a.w, b.y, b.w};
+      const int64_t c0 = p * 16;
+      if (row >= logical_rows) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = 0u;
+      } else if (c0 + 16 > logical_cols) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int64_t c = c0 + 2 * i;
+          if (c >= logical_cols) w[i] = 0u;
+          else if (c + 1 >= logical_cols) w[i] &= 0xffffu;
+        }
+      }
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst + m * per_matrix + row * cols + c0);
+      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+  }
+}
+
 // ---- Row-major -> BlockMajor{64,16}: TMA + ldmatrix.trans / stmatrix ------------
 // BlockMajor{64,16} (storage.rs:372-426) stores each 64-row band contiguously:
 // for every 16-column block, its four 16x16 row groups, each column-major.  A
@@ -672,6 +734,16 @@ extern "C" ipuc_status ipuc_unpack_f16(void *dst, const void *src, int32_t sourc
   else return fail(IPUC_ERR_INVALID_ARGUMENT, "unpack: source_order must be 0 (AMP-Output) or 1 (AMP-TransposedLeft)");
   if (matrices == 0 || physical_rows == 0) return IPUC_OK;
   const int64_t me = physical_rows * physical_columns;
+  if (source_order == 0 && physical_columns % 16 == 0 && aligned(src, 16) && aligned(dst, 16) && src != dst) {
+    const int64_t panels = physical_columns / 16;
+    const int64_t tiles = matrices * ((physical_rows + UNP_ROWS - 1) / UNP_ROWS) *
+                          ((panels + UNP_PANELS - 1) / UNP_PANELS);
+    const int64_t cap = (int64_t)sm_count() * 8, want = tiles;
+    unpack_amp_output_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, stream>>>(
+        static_cast<const uint16_t *>(src), static_cast<uint16_t *>(dst), matrices, physical_rows, physical_columns,
+        logical_rows, logical_columns);
+    return check_launch("unpack_amp_output_kernel");
+  }
   Side s{const_cast<void *>(src), order, physical_rows, physical_columns, physical_columns, me, 0, 0, 0};
   Side d{dst, IPUC_ORDER_ROW_MAJOR, physical_rows, physical_columns, physical_columns, me, 0, 0, 0};
   return launch_convert(s, d, logical_rows, logical_columns, matrices, stream);
