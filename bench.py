@@ -384,30 +384,38 @@ def profiled_traffic(kernel: str, share: float = 1.0):
 
 
 def measure_components(ipuc, torch, stream, hbm_gbs):
-    """Rearrange GB/s (config-5 weight tiles) and FP32 GEMM TFLOP/s (config 2),
-    reported beside the headline, not folded into it."""
+    """Layout-kernel GB/s (config-5 weight tiles), FP32 GEMM TFLOP/s (config 2) and
+    the config-5 block, reported beside the headline, not folded into it."""
     s = stream.cuda_stream
     out = {}
-    # row-major -> block-major {64,16}, 201M f16 elements
+    # Layout kernels on 201M f16 elements (4096 x 49152, the config-5 weight-tile
+    # volume): row-major -> AMP-Left / AMP-TransposedRight / BlockMajor{64,16}
+    # (rearrange_* codelets) and AMP-Output / AMP-TransposedLeft -> row-major
+    # (unpack_amp_f16).  GB/s counts one read and one write of every element.
     n = REARRANGE_ROWS * REARRANGE_COLS
+    R, C = REARRANGE_ROWS, REARRANGE_COLS
     src = torch.empty(n, dtype=torch.int16, device="cuda").random_(-30000, 30000)
     dst = torch.empty(n, dtype=torch.int16, device="cuda")
-    for target in (0, 2):
-        def run():
-            ipuc.call("ipuc_rearrange_f16", dst.data_ptr(), src.data_ptr(), 1, REARRANGE_ROWS, REARRANGE_ROWS, target,
-                      REARRANGE_COLS, REARRANGE_COLS, 64, 16, s)
+    layouts = [
+        ("rearrange_amp_left", "ipuc_rearrange_f16", (dst.data_ptr(), src.data_ptr(), 1, R, R, 0, C, C, 64, 16, s)),
+        ("rearrange_amp_transposed_right", "ipuc_rearrange_f16",
+         (dst.data_ptr(), src.data_ptr(), 1, R, R, 1, C, C, 64, 16, s)),
+        ("rearrange_block_major", "ipuc_rearrange_f16", (dst.data_ptr(), src.data_ptr(), 1, R, R, 2, C, C, 64, 16, s)),
+        ("unpack_amp_output", "ipuc_unpack_f16", (dst.data_ptr(), src.data_ptr(), 0, 1, R, R, C, C, s)),
+        ("unpack_amp_transposed_left", "ipuc_unpack_f16", (dst.data_ptr(), src.data_ptr(), 1, 1, R, R, C, C, s)),
+    ]
+    for name, fn, args in layouts:
         for _ in range(3):
-            run()
+            ipuc.call(fn, *args)
         a, b = torch.cuda.Event(True), torch.cuda.Event(True)
         a.record(stream)
         for _ in range(10):
-            run()
+            ipuc.call(fn, *args)
         b.record(stream)
         torch.cuda.synchronize()
         ms = a.elapsed_time(b) / 10
         gbs = 2 * n * 2 / (ms * 1e-3) / 1e9
-        out[f"rearrange_{'amp_left' if target == 0 else 'block_major'}"] = {
-            "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3)}
+        out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3)}
     del src, dst
     # FP32 GEMM 4096^3 (3xTF32)
     try:
