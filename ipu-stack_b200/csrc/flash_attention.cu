@@ -21,6 +21,14 @@
 // the final 1/denominator uses the same stale max.
 // Head dims up to 128 (multiple of 8) are zero-padded to 128 by the TMA; key
 // and query tails are masked.  Every wait is bounded (error word, no trap).
+//
+// Launch partition: from 512 query rows up, CTA pairs (cta_group::2, M = 256
+// over the pair, each CTA loading half of every K and V tile) take 512-row
+// units in whole waves; a last wave at most half full runs as split clusters
+// (kSplit: two CTAs per 256-row unit, each over half the key tiles, merged
+// through distributed shared memory).  Q/K/V/O are addressed through 4-D maps
+// (head_dim, heads, rows, batch), so the same kernels serve [streams][rows][d]
+// tensors (heads = 1) and unsplit [batch][rows][heads * d] projections.
 #include <math.h>
 
 #include "common.cuh"
