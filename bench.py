@@ -307,8 +307,10 @@ def run_ours(args):
         comps = measure_components(ipuc, torch, stream, hbm)
     if world > 1:
         barrier(world)
+        gather = gather_outputs(torch, world, y, o)
         tp = transformer_block_tp(torch, rank, world)
         if rank == 0:
+            comps["gather_outputs"] = gather
             comps["transformer_block_tp"] = tp
 
     # ---- CPU baseline (oracle, bounded sample, rank 0 at N=1) ----
@@ -483,6 +485,37 @@ def transformer_block(ipuc, torch, stream):
            "steps": sess.plan.count("\n")}
     sess.close()
     return out
+
+
+def gather_outputs(torch, world, y, o):
+    """The optional final exchange of the sharded step: NCCL all-gather of every
+    rank's GEMM output columns and attention streams onto every GPU (over NVLink
+    on one box).  Not part of the headline (consumers that are themselves
+    sharded need no gather).  Device time, max over ranks; bus bandwidth
+    (N-1)/N x gathered bytes / time."""
+    import torch.distributed as dist
+    gy = torch.empty((world,) + tuple(y.shape), dtype=y.dtype, device=y.device)
+    go = torch.empty((world,) + tuple(o.shape), dtype=o.dtype, device=o.device)
+    stream = torch.cuda.current_stream()
+
+    def run():
+        dist.all_gather_into_tensor(gy, y.contiguous())
+        dist.all_gather_into_tensor(go, o.contiguous())
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(5):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / 5, world)
+    total = (gy.numel() + go.numel()) * gy.element_size()
+    del gy, go
+    return {"ms": round(ms, 4), "gathered_bytes": total,
+            "bus_GB/s": round((world - 1) / world * total / (ms * 1e-3) / 1e9, 1), "collective": "NCCL all_gather"}
 
 
 def transformer_block_tp(torch, rank, world):
