@@ -54,6 +54,12 @@ ipuc_status ipug_set_outputs(ipug_graph *g, const int32_t *values, int32_t count
 /* Shape of a value: returns its rank (<= 8 dims written), or -1. */
 int32_t ipug_value_shape(const ipug_graph *g, int32_t value, uint32_t *dims);
 
+/* The lowering ipug_session_open would perform (one line per step, as
+ * ipug_session_plan), computed on the host without a device or allocation.
+ * IPUC_ERR_INVALID_ARGUMENT if buf is too small (*needed = bytes required);
+ * lowering errors (IPUC_ERR_UNSUPPORTED) as ipug_session_open reports them. */
+ipuc_status ipug_graph_plan(const ipug_graph *g, char *buf, uint64_t size, uint64_t *needed);
+
 /* Session: lower the graph for `device`, allocate every value's buffer. */
 ipug_session *ipug_session_open(const ipug_graph *g, int32_t device, ipuc_status *status);
 void ipug_session_close(ipug_session *s);

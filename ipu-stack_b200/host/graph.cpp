@@ -132,6 +132,9 @@ struct ipug_session {
   std::vector<Step> steps;
   std::string plan;
   ~ipug_session() {
+    bool any = false;
+    for (void *p : buffers) any = any || p != nullptr;
+    if (!any) return;  // a plan-only lowering holds no device memory
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(device);
@@ -143,7 +146,8 @@ struct ipug_session {
 
 namespace {
 
-ipuc_status lower(const ipug_graph &g, ipug_session &s) {
+// allocate = false lowers without touching a device (ipug_graph_plan).
+ipuc_status lower(const ipug_graph &g, ipug_session &s, bool allocate = true) {
   const size_t nv = g.values.size();
   std::vector<std::vector<int32_t>> consumers(nv);
   for (size_t i = 0; i < g.ops.size(); ++i)
@@ -387,6 +391,7 @@ ipuc_status lower(const ipug_graph &g, ipug_session &s) {
   s.plan = plan.str();
   // Buffers: every value except the results of ops fused into a consumer.
   s.buffers.assign(nv, nullptr);
+  if (!allocate) return IPUC_OK;
   for (size_t v = 0; v < nv; ++v) {
     const Value &val = g.values[v];
     if (val.kind == 2 && fused_into_next[val.producer]) continue;
@@ -596,6 +601,19 @@ ipug_session *ipug_session_open(const ipug_graph *g, int32_t device, ipuc_status
 }
 
 void ipug_session_close(ipug_session *s) { delete s; }
+
+ipuc_status ipug_graph_plan(const ipug_graph *g, char *buf, uint64_t size, uint64_t *needed) {
+  if (!g) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "graph_plan: null graph");
+  ipug_session s;
+  s.graph = g;
+  const ipuc_status st = lower(*g, s, false);
+  if (st != IPUC_OK) return st;
+  if (needed) *needed = s.plan.size() + 1;
+  if (!buf || size < s.plan.size() + 1)
+    return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "graph_plan: buffer too small");
+  std::memcpy(buf, s.plan.c_str(), s.plan.size() + 1);
+  return IPUC_OK;
+}
 
 static ipuc_status check_value(ipug_session *s, int32_t value, uint64_t bytes) {
   if (!s || !s->graph->valid(value)) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session: unknown value");

@@ -46,6 +46,7 @@ _G_SIGS = {
     "ipug_session_profile": (ctypes.c_int32, [_vp, _vp, ctypes.c_char_p, ctypes.c_uint64,
                                               ctypes.POINTER(ctypes.c_uint64)]),
     "ipug_session_plan": (ctypes.c_char_p, [_vp]),
+    "ipug_graph_plan": (ctypes.c_int32, [_vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
 }
 _bound = False
 
@@ -156,6 +157,19 @@ class ComputeGraph:
         if st != OK:
             raise GraphError(_lib().ipuc_last_error_string().decode())
         self.outputs = outs
+
+    def plan(self) -> str:
+        """The per-GPU lowering (one line per step), computed on the host
+        without a device: the plan a Session of this graph would run."""
+        need = ctypes.c_uint64(0)
+        glib().ipug_graph_plan(self._g, None, 0, ctypes.byref(need))
+        if need.value == 0:
+            raise GraphError(_lib().ipuc_last_error_string().decode())
+        buf = ctypes.create_string_buffer(need.value)
+        st = glib().ipug_graph_plan(self._g, buf, need.value, ctypes.byref(need))
+        if st != OK:
+            raise IpucError("ipug_graph_plan", st, _lib().ipuc_last_error_string().decode())
+        return buf.value.decode()
 
     def value_shape(self, v: int) -> tuple:
         dims = (ctypes.c_uint32 * 8)()
