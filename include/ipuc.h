@@ -103,6 +103,16 @@ ipuc_status ipuc_gemm_f16(void *c, const void *a, const void *b, int64_t m, int6
                           int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags,
                           ipuc_stream stream);
 
+/* GEMM with an epilogue addend (the graph's Gemm -> Add, the residual add):
+ *   C[m x n] = epilogue(A . B + D)
+ * with D [m x n] at leading dimension ld_addend, of C's precision (f16, or f32
+ * with IPUC_GEMM_OUT_F32); D may equal C.  Epilogue order: acc + D -> round
+ * to C's precision -> GELU (with IPUC_GEMM_EPILOGUE_GELU) -> store.  Otherwise
+ * as ipuc_gemm_f16 (IPUC_GEMM_ACCUMULATE is implied). */
+ipuc_status ipuc_gemm_f16_addend(void *c, const void *a, const void *b, int64_t m, int64_t n, int64_t k,
+                                 int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, const void *addend,
+                                 int64_t ld_addend, ipuc_stream stream);
+
 /* Batched form: `batch` independent GEMMs at the given element strides
  * (batched-gemm-smoke, crates/ipu-tests/src/main.rs:201-220). */
 ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t batch,

@@ -35,6 +35,8 @@ constexpr int GROUP_M = 16;
 
 struct GemmParams {
   void *c;
+  const void *add;          // what IPUC_GEMM_ACCUMULATE adds: C itself, or a separate addend
+  int64_t ld_add, stride_add;
   int64_t m, n, k, batch;
   int64_t ldc, stride_c;
   int32_t tiles_m, tiles_n, k_blocks;
@@ -67,12 +69,14 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int b, int64_t 
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
   if (out_f32) {
     float *cp = static_cast<float *>(p.c) + b * p.stride_c + row * p.ldc + col0;
+    const float *ap = static_cast<const float *>(p.add) + b * p.stride_add + row * p.ld_add + col0;
     if (full_chunk) {
       float4 *c4 = reinterpret_cast<float4 *>(cp);
       if (accumulate) {
+        const float4 *a4 = reinterpret_cast<const float4 *>(ap);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float4 o = c4[j];
+          const float4 o = a4[j];
           v[4 * j] += o.x; v[4 * j + 1] += o.y; v[4 * j + 2] += o.z; v[4 * j + 3] += o.w;
         }
       }
@@ -85,19 +89,21 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int b, int64_t 
     } else {
       for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
         float x = v[j];
-        if (accumulate) x += cp[j];
+        if (accumulate) x += ap[j];
         if (gelu) x = gelu_f32(x);
         cp[j] = x;
       }
     }
   } else {
     uint16_t *cp = static_cast<uint16_t *>(p.c) + b * p.stride_c + row * p.ldc + col0;
+    const uint16_t *ap = static_cast<const uint16_t *>(p.add) + b * p.stride_add + row * p.ld_add + col0;
     if (full_chunk) {
       uint4 *c4 = reinterpret_cast<uint4 *>(cp);
       if (accumulate) {
+        const uint4 *a4 = reinterpret_cast<const uint4 *>(ap);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint4 o = c4[j];
+          const uint4 o = a4[j];
           const uint16_t *h = reinterpret_cast<const uint16_t *>(&o);
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[8 * j + e] += h2f(h[e]);
@@ -115,7 +121,7 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int b, int64_t 
     } else {
       for (int j = 0; j < 32 && col0 + j < p.n; ++j) {
         float x = v[j];
-        if (accumulate) x += h2f(cp[j]);
+        if (accumulate) x += h2f(ap[j]);
         uint32_t h = f2h(x);
         if (gelu) h = gelu_h2(h) & 0xffffu;
         cp[j] = (uint16_t)h;
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(192, 1)
     const bool out_f32 = (p.flags & IPUC_GEMM_OUT_F32) != 0;
     const bool accumulate = (p.flags & IPUC_GEMM_ACCUMULATE) != 0;
     const bool gelu = (p.flags & IPUC_GEMM_EPILOGUE_GELU) != 0;
-    const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0);
+    const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0) && (p.ld_add % 8 == 0) && (p.stride_add % 8 == 0);
     uint32_t local = 0;
     for (int64_t t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1u, use = local >> 1;
@@ -413,7 +419,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const bool out_f32 = (p.flags & IPUC_GEMM_OUT_F32) != 0;
     const bool accumulate = (p.flags & IPUC_GEMM_ACCUMULATE) != 0;
     const bool gelu = (p.flags & IPUC_GEMM_EPILOGUE_GELU) != 0;
-    const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0);
+    const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0) && (p.ld_add % 8 == 0) && (p.stride_add % 8 == 0);
     uint32_t local = 0;
     for (int64_t t = pair; t < p.num_tiles; t += pairs, ++local) {
       const uint32_t buf = local & 1u, use = local >> 1;
@@ -451,7 +457,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 
 ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch, int64_t m, int64_t n, int64_t k,
                             int64_t lda, int64_t ldb, int64_t ldc, int64_t sa, int64_t sb, int64_t sc,
-                            uint32_t flags, cudaStream_t stream) {
+                            uint32_t flags, cudaStream_t stream, const void *addend = nullptr, int64_t ld_add = 0) {
   IPUC_CHECK_ARG(m >= 0 && n >= 0 && k >= 0 && batch >= 0, "gemm_f16: negative extent");
   IPUC_CHECK_ARG((flags & ~0xfu) == 0, "gemm_f16: unknown flag");
   if (m == 0 || n == 0 || batch == 0) return IPUC_OK;
@@ -472,6 +478,9 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
   if (st != IPUC_OK) return st;
   GemmParams p;
   p.c = c;
+  p.add = addend ? addend : c;
+  p.ld_add = addend ? ld_add : ldc;
+  p.stride_add = addend ? 0 : (batch > 1 ? sc : 0);
   p.m = m; p.n = n; p.k = k; p.batch = batch;
   p.ldc = ldc;
   p.stride_c = batch > 1 ? sc : 0;
@@ -522,6 +531,16 @@ using namespace ipuc;
 extern "C" ipuc_status ipuc_gemm_f16(void *c, const void *a, const void *b, int64_t m, int64_t n, int64_t k,
                                      int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags, ipuc_stream stream) {
   return launch_gemm_f16(c, a, b, 1, m, n, k, lda, ldb, ldc, 0, 0, 0, flags, stream);
+}
+
+extern "C" ipuc_status ipuc_gemm_f16_addend(void *c, const void *a, const void *b, int64_t m, int64_t n, int64_t k,
+                                            int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags,
+                                            const void *addend, int64_t ld_addend, ipuc_stream stream) {
+  IPUC_CHECK_ARG(addend != nullptr, "gemm_f16_addend: null addend");
+  IPUC_CHECK_ARG(ld_addend >= n, "gemm_f16_addend: addend leading dimension too small");
+  IPUC_CHECK_ALIGN(aligned(addend, 16), "gemm_f16_addend: addend must be 16-byte aligned");
+  return launch_gemm_f16(c, a, b, 1, m, n, k, lda, ldb, ldc, 0, 0, 0, flags | IPUC_GEMM_ACCUMULATE, stream, addend,
+                         ld_addend);
 }
 
 extern "C" ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t batch, int64_t m,

@@ -109,6 +109,7 @@ struct Step {
   std::vector<int32_t> op_ids;
   // value ids
   int32_t out = -1, in0 = -1, in1 = -1, in2 = -1;
+  int32_t addend = -1;  // Gemm: value the epilogue adds (the fused Add's other operand)
   // gemm
   int64_t batch = 1, m = 0, n = 0, k = 0;
   uint32_t flags = 0;
@@ -258,20 +259,25 @@ ipuc_status lower(const ipug_graph &g, ipug_session &s, bool allocate = true) {
         if (fused_gemm[i] >= 0) {
           const Op &gm = g.ops[fused_gemm[i]];
           const int32_t other = op.inputs[0] == gm.result ? op.inputs[1] : op.inputs[0];
-          Step cp;
-          cp.kind = StepKind::Copy;
-          cp.op_ids.push_back((int32_t)i);
-          cp.in0 = other;
-          cp.out = op.result;
-          cp.count = numel(g.values[op.result].shape);
-          cp.bytes = 4.0 * cp.count;
-          cp.label = "copy(addend)";
-          s.steps.push_back(cp);
           st.kind = StepKind::Gemm;
           st.op_ids.insert(st.op_ids.begin(), fused_gemm[i]);
           rc = gemm_step(gm, st);
           st.flags |= IPUC_GEMM_ACCUMULATE;
           st.label = "gemm_f16+add";
+          if (st.batch == 1) {
+            st.addend = other;  // the GEMM epilogue reads it: no copy
+          } else {
+            // Batched: copy the addend into the output, then accumulate onto it.
+            Step cp;
+            cp.kind = StepKind::Copy;
+            cp.op_ids.push_back((int32_t)i);
+            cp.in0 = other;
+            cp.out = op.result;
+            cp.count = numel(g.values[op.result].shape);
+            cp.bytes = 4.0 * cp.count;
+            cp.label = "copy(addend)";
+            s.steps.push_back(cp);
+          }
         } else {
           st.kind = StepKind::Add;
           const auto &a = g.values[op.inputs[0]].shape, &b = g.values[op.inputs[1]].shape;
@@ -407,6 +413,9 @@ ipuc_status run_step(ipug_session &s, const Step &st, cudaStream_t stream) {
   switch (st.kind) {
     case StepKind::Gemm: {
       const int64_t lda = st.k, ldb = (st.flags & IPUC_GEMM_B_TRANSPOSED) ? st.k : st.n, ldc = st.n;
+      if (st.batch == 1 && st.addend >= 0)
+        return ipuc_gemm_f16_addend(P(st.out), P(st.in0), P(st.in1), st.m, st.n, st.k, lda, ldb, ldc, st.flags,
+                                    P(st.addend), st.n, stream);
       if (st.batch == 1)
         return ipuc_gemm_f16(P(st.out), P(st.in0), P(st.in1), st.m, st.n, st.k, lda, ldb, ldc, st.flags, stream);
       return ipuc_gemm_f16_batched(P(st.out), P(st.in0), P(st.in1), st.batch, st.m, st.n, st.k, lda, ldb, ldc,

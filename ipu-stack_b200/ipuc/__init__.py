@@ -40,6 +40,7 @@ SIGNATURES = {
     "ipuc_fill_zero": (_i32, [_vp, _u64, _vp]),
     "ipuc_selftest_bounded_wait": (_i32, [_u64, _vp]),
     "ipuc_gemm_f16": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _u32, _vp]),
+    "ipuc_gemm_f16_addend": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _u32, _vp, _i64, _vp]),
     "ipuc_gemm_f16_batched": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                      _u32, _vp]),
     "ipuc_gemm_f32_workspace_bytes": (_u64, [_i64, _i64, _i64]),
@@ -148,6 +149,17 @@ def gemm_f16(c, a, b, m, n, k, lda=None, ldb=None, ldc=None, flags=0, stream=Non
     ldb = (k if bt else n) if ldb is None else ldb
     ldc = n if ldc is None else ldc
     call("ipuc_gemm_f16", _ptr(c), _ptr(a), _ptr(b), m, n, k, lda, ldb, ldc, flags, _stream(stream))
+
+
+def gemm_f16_addend(c, a, b, m, n, k, addend, ld_addend=None, lda=None, ldb=None, ldc=None, flags=0, stream=None):
+    """C = epilogue(A.B + addend): the Gemm -> Add fusion with the addend read by the epilogue."""
+    bt = bool(flags & GEMM_B_TRANSPOSED)
+    lda = k if lda is None else lda
+    ldb = (k if bt else n) if ldb is None else ldb
+    ldc = n if ldc is None else ldc
+    ld_addend = n if ld_addend is None else ld_addend
+    call("ipuc_gemm_f16_addend", _ptr(c), _ptr(a), _ptr(b), m, n, k, lda, ldb, ldc, flags, _ptr(addend), ld_addend,
+         _stream(stream))
 
 
 def gemm_f16_batched(c, a, b, batch, m, n, k, flags=0, stream=None):

@@ -6,8 +6,8 @@ by columns (whole heads per rank), attention is head-local, the output
 projection is split by rows, the MLP up-projection by columns and the
 down-projection by rows, so each rank ends each half of the block with a
 partial sum of the full activation and one all-reduce per half combines them.
-The residual adds are folded into rank 0's partial sum (its GEMM accumulates
-onto the residual), so each all-reduce yields the residual sum directly.
+The residual adds are folded into rank 0's partial sum (its GEMM epilogue adds
+the residual), so each all-reduce yields the residual sum directly.
 
 Compute is the library's kernels (ipuc_gemm_f16 with the fused GELU/accumulate
 epilogues, and ipuc_flash_attention_heads_f16 reading the local heads straight
@@ -19,7 +19,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-from . import GEMM_ACCUMULATE, GEMM_EPILOGUE_GELU, F16, call
+from . import GEMM_EPILOGUE_GELU, F16, call
 
 
 @dataclass(frozen=True)
@@ -80,8 +80,12 @@ class TensorParallelBlock:
         self.w1.copy_(weights["w1"][:, f0:f1])
         self.w2.copy_(weights["w2"][f0:f1, :])
 
-    def _gemm(self, c, a, b, m, n, k, flags, s):
-        call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, flags, s)
+    def _gemm(self, c, a, b, m, n, k, flags, s, addend=None):
+        if addend is None:
+            call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, flags, s)
+        else:  # the epilogue adds `addend` (the residual): no copy
+            call("ipuc_gemm_f16_addend", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, flags,
+                 addend.data_ptr(), n, s)
 
     def _all_reduce(self, t):
         import torch.distributed as dist
@@ -99,16 +103,12 @@ class TensorParallelBlock:
         # Local heads read in place from [B, S, hl * dh] and written merged.
         call("ipuc_flash_attention_heads_f16", self.a.data_ptr(), F16, self.qf.data_ptr(), self.kf.data_ptr(),
              self.vf.data_ptr(), self.B, self.hl, self.S, self.S, self.dh, 0.0, s)
-        # h = x + sum over ranks of a_r Wo_r (rank 0 accumulates onto x).
-        if self.shard.adds_residual:
-            self.h.copy_(x)
-        self._gemm(self.h, self.a, self.wo, T, d, self.dl, GEMM_ACCUMULATE if self.shard.adds_residual else 0, s)
+        # h = x + sum over ranks of a_r Wo_r (rank 0's epilogue adds x).
+        self._gemm(self.h, self.a, self.wo, T, d, self.dl, 0, s, x if self.shard.adds_residual else None)
         self._all_reduce(self.h)
         # y = h + sum over ranks of GELU(h W1_r) W2_r.
         self._gemm(self.u, self.h, self.w1, T, self.fl, d, GEMM_EPILOGUE_GELU, s)
-        if self.shard.adds_residual:
-            self.y.copy_(self.h)
-        self._gemm(self.y, self.u, self.w2, T, d, self.fl, GEMM_ACCUMULATE if self.shard.adds_residual else 0, s)
+        self._gemm(self.y, self.u, self.w2, T, d, self.fl, 0, s, self.h if self.shard.adds_residual else None)
         self._all_reduce(self.y)
         return self.y
 

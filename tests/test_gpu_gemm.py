@@ -86,6 +86,37 @@ def test_gemm_epilogues(flags, with_c):
         assert ok, msg
 
 
+@pytest.mark.parametrize("m,n,k,flags,ld_pad", [
+    (384, 640, 320, 0, 0), (300, 520, 256, ipuc.GEMM_EPILOGUE_GELU, 8), (2048, 2048, 1024, 0, 0),
+    (384, 640, 320, ipuc.GEMM_OUT_F32, 4), (1000, 136, 72, ipuc.GEMM_B_TRANSPOSED, 16)])
+def test_gemm_addend_epilogue(m, n, k, flags, ld_pad):
+    """ipuc_gemm_f16_addend: C = epilogue(A.B + D) with D a separate tensor (the
+    fused residual add), read at its own leading dimension; C is not read."""
+    bt = bool(flags & ipuc.GEMM_B_TRANSPOSED)
+    out_f32 = bool(flags & ipuc.GEMM_OUT_F32)
+    a = oracle.f16_bits(seeded_normal(m, (m, k), 0.1))
+    b = oracle.f16_bits(seeded_normal(n, (n, k) if bt else (k, n), 0.1))
+    ld = n + ld_pad
+    d = seeded_normal(k, (m, ld))
+    d = d if out_f32 else oracle.quantize_f16(d)
+    ref = oracle.gemm(f16_of(a), f16_of(b), False, bt) + d[:, :n]
+    if not out_f32:
+        ref = oracle.quantize_f16(ref)
+    if flags & ipuc.GEMM_EPILOGUE_GELU:
+        ref = oracle.quantize_f16(oracle.gelu(ref))
+    if out_f32:
+        c, dd = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda"), dev_f32(d)
+    else:
+        c, dd = empty_u16(m * n), dev_u16(oracle.f16_bits(d))
+    ipuc.gemm_f16_addend(c, dev_u16(a), dev_u16(b), m, n, k, dd, ld_addend=ld, flags=flags)
+    got = (host_f32(c) if out_f32 else f16_of(host_u16(c))).reshape(m, n)
+    if out_f32:
+        assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-5
+    else:
+        ok, msg = f16_close(got, ref)
+        assert ok, msg
+
+
 def test_gemm_splitk_partials_reduce():
     """Config-3 lowering shape: split-K into 4 f32 partials (GEMM with
     OUT_F32 on K slices), combined by reduce_add, then GELU."""
