@@ -165,7 +165,9 @@ def run_ours(args):
 
     n0, nw = shard(MLP_N, world, rank)
     s0, ns = shard(ATT_B * ATT_H, world, rank)
-    x = torch.randn((MLP_M, MLP_K), generator=g, device=dev, dtype=torch.float32).half()
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(1234)  # X is one tensor for the whole job: the same on every rank
+    x = torch.randn((MLP_M, MLP_K), generator=gx, device=dev, dtype=torch.float32).half()
     w = (torch.randn((MLP_K, nw), generator=g, device=dev, dtype=torch.float32) * (1.0 / 64.0)).half()
     y = torch.empty((MLP_M, nw), device=dev, dtype=torch.float16)
     q = torch.randn((ns, ATT_S, ATT_D), generator=g, device=dev, dtype=torch.float32).half()
@@ -239,6 +241,13 @@ def run_ours(args):
     comp_ev = [torch.cuda.Event() for _ in range(n_ch)]
     out_ev = [torch.cuda.Event() for _ in range(n_ch)]
     w_ev = torch.cuda.Event()
+    # X is replicated (every rank's GEMM shard reads all of it): at N>1 each rank
+    # uploads a 1/N row slice of every chunk and an NCCL all-gather over NVLink
+    # assembles the chunk, so each byte of X crosses PCIe once per step for the
+    # whole job instead of once per rank.
+    gather_x = world > 1 and not args.e2e_replicated_x and all((r1 - r0) % world == 0 for r0, r1 in g_chunks)
+    if gather_x:
+        import torch.distributed as dist
 
     def e2e_step():
         with torch.cuda.stream(s_in):
@@ -247,7 +256,14 @@ def run_ours(args):
             w_ev.record(s_in)
             for i, (r0, r1) in enumerate(g_chunks):
                 s_in.wait_event(comp_ev[i])
-                x[r0:r1].copy_(hx[r0:r1], non_blocking=True)
+                if gather_x:
+                    # this rank uploads its 1/N of the chunk's rows; NVLink brings the rest
+                    p = (r1 - r0) // world
+                    a0 = r0 + rank * p
+                    x[a0:a0 + p].copy_(hx[a0:a0 + p], non_blocking=True)
+                    dist.all_gather_into_tensor(x[r0:r1], x[a0:a0 + p])
+                else:
+                    x[r0:r1].copy_(hx[r0:r1], non_blocking=True)
                 in_ev[i].record(s_in)
             for j, (c0, c1) in enumerate(a_chunks):
                 i = len(g_chunks) + j
@@ -297,7 +313,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
-    h2d = sum(t.numel() * t.element_size() for t in (hx, hw, hq, hk, hv))
+    h2d = sum(t.numel() * t.element_size() for t in (hw, hq, hk, hv))
+    h2d += hx.numel() * hx.element_size() // (world if gather_x else 1)
     d2h = sum(t.numel() * t.element_size() for t in (hy, ho))
 
     # ---- supplementary components (not in value) ----
@@ -689,6 +706,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
+    ap.add_argument("--e2e-replicated-x", action="store_true",
+                    help="at N>1 every rank uploads all of X in the e2e step (no NVLink all-gather)")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--profile", choices=["gemm", "attention", "attention8", "rearrange", "rearrange_amp_left",
                                           "gemm_f32"],
