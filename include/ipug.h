@@ -76,6 +76,57 @@ ipuc_status ipug_session_run(ipug_session *s, ipuc_stream stream);
  * (crates/ipu-package/src/lib.rs:193-265).  Returns IPUC_ERR_INVALID_ARGUMENT
  * if buf is too small (the required size is written to *needed). */
 ipuc_status ipug_session_profile(ipug_session *s, ipuc_stream stream, char *buf, uint64_t size, uint64_t *needed);
+/* ---- Profile reports in the reference's Cap'n Proto format ----
+ * The message is a `Profile` of schemas/profile.capnp (schema version 5,
+ * written by ProfileReport::write, crates/ipu-package/src/lib.rs:198-222):
+ * clockHz, and per tile (here: per GPU) a list of CycleSamples, each a Step of
+ * schemas/profile_common.capnp with a start and end cycle.  The bytes are the
+ * standard single-segment stream framing (capnp::serialize::write_message), so
+ * the reference's ProfileReport::read and `ipu-profile query` read them. */
+typedef enum ipug_step_kind {
+  IPUG_STEP_EXCHANGE = 0,
+  IPUG_STEP_COMPUTE = 1,
+  IPUG_STEP_SYNCHRONIZATION = 2,
+  IPUG_STEP_IDLE = 3
+} ipug_step_kind;
+
+typedef struct ipug_exchange_activity {
+  uint32_t kind; /* 0 send, 1 receive, 2 partnerBusy (ExchangeActivityKind) */
+  uint32_t start_cycle, end_cycle;
+} ipug_exchange_activity;
+
+typedef struct ipug_profile_sample {
+  uint32_t local_index, phase, epoch;
+  uint32_t kind;                 /* ipug_step_kind */
+  const char *operation;         /* "operation.<index>" in the reference; NULL = "" */
+  const char *kernel;            /* NULL = "" */
+  const char *const *metadata;   /* metadata_count (name, value) pairs: 2*count strings */
+  uint32_t metadata_count;
+  const ipug_exchange_activity *activities;
+  uint32_t activity_count;
+  uint32_t exchange_event_cycles;
+  uint32_t start_cycle, end_cycle;
+} ipug_profile_sample;
+
+typedef struct ipug_profile_tile {
+  uint32_t physical_tile;
+  const ipug_profile_sample *samples;
+  uint64_t sample_count;
+} ipug_profile_tile;
+
+/* Encode a Profile message.  IPUC_ERR_INVALID_ARGUMENT if buf is too small
+ * (the required size is written to *needed) or a kind is out of range. */
+ipuc_status ipug_profile_encode(uint64_t clock_hz, const ipug_profile_tile *tiles, uint64_t tile_count, void *buf,
+                                uint64_t size, uint64_t *needed);
+/* Run the session once with a CUDA event around every lowered step and write
+ * the timings as a one-tile Profile message (physical tile = `physical_tile`,
+ * normally the GPU's rank): clockHz 1e9, so a cycle is one nanosecond from the
+ * first event; one Compute step per lowered step, operation "operation.<id>"
+ * of its first graph operation, kernel = the step's kernel, metadata
+ * "operations" (all fused op ids), "flop"/"tflops" or "bytes"/"gbs", "device". */
+ipuc_status ipug_session_profile_capnp(ipug_session *s, ipuc_stream stream, uint32_t physical_tile, void *buf,
+                                       uint64_t size, uint64_t *needed);
+
 /* Human-readable lowered plan (one line per step). */
 const char *ipug_session_plan(const ipug_session *s);
 

@@ -667,45 +667,110 @@ ipuc_status ipug_session_run(ipug_session *s, ipuc_stream stream) {
   return IPUC_OK;
 }
 
+}  // extern "C"
+
+// Run every lowered step once with a CUDA event on each boundary; t[i] is the
+// time of boundary i in ms after boundary 0 (t.size() == steps + 1).
+static ipuc_status time_steps(ipug_session *s, ipuc_stream stream, std::vector<double> &t, const char *who) {
+  DeviceGuard guard(s->device);
+  std::vector<cudaEvent_t> ev(s->steps.size() + 1, nullptr);
+  ipuc_status rc = IPUC_OK;
+  for (auto &e : ev)
+    if (rc == IPUC_OK && cudaEventCreate(&e) != cudaSuccess) rc = ipuc::fail(IPUC_ERR_CUDA, std::string(who) + ": cudaEventCreate");
+  if (rc == IPUC_OK) {
+    cudaEventRecord(ev[0], stream);
+    for (size_t i = 0; i < s->steps.size() && rc == IPUC_OK; ++i) {
+      rc = run_step(*s, s->steps[i], stream);
+      cudaEventRecord(ev[i + 1], stream);
+    }
+  }
+  if (rc == IPUC_OK && cudaEventSynchronize(ev.back()) != cudaSuccess)
+    rc = ipuc::fail(IPUC_ERR_CUDA, std::string(who) + ": event synchronize failed");
+  if (rc == IPUC_OK) {
+    t.assign(ev.size(), 0.0);
+    for (size_t i = 1; i < ev.size(); ++i) {
+      float ms = 0.0f;
+      cudaEventElapsedTime(&ms, ev[0], ev[i]);
+      t[i] = ms;
+    }
+  }
+  for (auto &e : ev)
+    if (e) cudaEventDestroy(e);
+  return rc;
+}
+
+extern "C" {
+
 ipuc_status ipug_session_profile(ipug_session *s, ipuc_stream stream, char *buf, uint64_t size, uint64_t *needed) {
   if (!s) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session_profile: null session");
-  DeviceGuard guard(s->device);
-  std::vector<cudaEvent_t> ev(s->steps.size() + 1);
-  for (auto &e : ev)
-    if (cudaEventCreate(&e) != cudaSuccess) return ipuc::fail(IPUC_ERR_CUDA, "session_profile: cudaEventCreate");
-  ipuc_status rc = IPUC_OK;
-  cudaEventRecord(ev[0], stream);
-  for (size_t i = 0; i < s->steps.size() && rc == IPUC_OK; ++i) {
-    rc = run_step(*s, s->steps[i], stream);
-    cudaEventRecord(ev[i + 1], stream);
-  }
-  std::ostringstream o;
-  if (rc == IPUC_OK && cudaEventSynchronize(ev.back()) == cudaSuccess) {
-    o << "{\"device\": " << s->device << ", \"steps\": [";
-    double total = 0.0;
-    for (size_t i = 0; i < s->steps.size(); ++i) {
-      float ms = 0.0f;
-      cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
-      total += ms;
-      const Step &st = s->steps[i];
-      o << (i ? ", " : "") << "{\"step\": " << i << ", \"kernel\": \"" << st.label << "\", \"ops\": [";
-      for (size_t j = 0; j < st.op_ids.size(); ++j) o << (j ? ", " : "") << st.op_ids[j];
-      o << "], \"ms\": " << ms;
-      if (st.flop > 0) o << ", \"flop\": " << st.flop << ", \"tflops\": " << st.flop / (ms * 1e-3) / 1e12;
-      if (st.bytes > 0) o << ", \"bytes\": " << st.bytes << ", \"gbs\": " << st.bytes / (ms * 1e-3) / 1e9;
-      o << "}";
-    }
-    o << "], \"total_ms\": " << total << "}";
-  } else if (rc == IPUC_OK) {
-    rc = ipuc::fail(IPUC_ERR_CUDA, "session_profile: event synchronize failed");
-  }
-  for (auto &e : ev) cudaEventDestroy(e);
+  std::vector<double> t;
+  const ipuc_status rc = time_steps(s, stream, t, "session_profile");
   if (rc != IPUC_OK) return rc;
+  std::ostringstream o;
+  o << "{\"device\": " << s->device << ", \"steps\": [";
+  for (size_t i = 0; i < s->steps.size(); ++i) {
+    const double ms = t[i + 1] - t[i];
+    const Step &st = s->steps[i];
+    o << (i ? ", " : "") << "{\"step\": " << i << ", \"kernel\": \"" << st.label << "\", \"ops\": [";
+    for (size_t j = 0; j < st.op_ids.size(); ++j) o << (j ? ", " : "") << st.op_ids[j];
+    o << "], \"ms\": " << ms;
+    if (st.flop > 0) o << ", \"flop\": " << st.flop << ", \"tflops\": " << st.flop / (ms * 1e-3) / 1e12;
+    if (st.bytes > 0) o << ", \"bytes\": " << st.bytes << ", \"gbs\": " << st.bytes / (ms * 1e-3) / 1e9;
+    o << "}";
+  }
+  o << "], \"total_ms\": " << t.back() << "}";
   const std::string js = o.str();
   if (needed) *needed = js.size() + 1;
   if (!buf || size < js.size() + 1) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session_profile: buffer too small");
   std::memcpy(buf, js.c_str(), js.size() + 1);
   return IPUC_OK;
+}
+
+ipuc_status ipug_session_profile_capnp(ipug_session *s, ipuc_stream stream, uint32_t physical_tile, void *buf,
+                                       uint64_t size, uint64_t *needed) {
+  if (!s) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session_profile_capnp: null session");
+  std::vector<double> t;
+  const ipuc_status rc = time_steps(s, stream, t, "session_profile_capnp");
+  if (rc != IPUC_OK) return rc;
+  const size_t n = s->steps.size();
+  // Strings the samples point at; reserved so the pointers stay put.
+  std::vector<std::string> text;
+  text.reserve(n * 16);
+  std::vector<std::vector<const char *>> meta(n);
+  std::vector<ipug_profile_sample> samples(n);
+  auto keep = [&text](std::string v) { text.push_back(std::move(v)); return text.back().c_str(); };
+  auto num = [](double v) { std::ostringstream o; o << v; return o.str(); };
+  auto cycles = [](double ms) {  // 1 cycle = 1 ns at clockHz 1e9
+    const double c = std::llround(ms * 1e6);
+    return static_cast<uint32_t>(c < 0 ? 0 : (c > 4294967295.0 ? 4294967295.0 : c));
+  };
+  for (size_t i = 0; i < n; ++i) {
+    const Step &st = s->steps[i];
+    const double ms = t[i + 1] - t[i];
+    std::string ops;
+    for (size_t j = 0; j < st.op_ids.size(); ++j) ops += (j ? "," : "") + std::to_string(st.op_ids[j]);
+    auto &m = meta[i];
+    m = {keep("operations"), keep(ops), keep("device"), keep(std::to_string(s->device))};
+    if (st.flop > 0) {
+      m.insert(m.end(), {keep("flop"), keep(num(st.flop)), keep("tflops"), keep(num(st.flop / (ms * 1e-3) / 1e12))});
+    }
+    if (st.bytes > 0) {
+      m.insert(m.end(), {keep("bytes"), keep(num(st.bytes)), keep("gbs"), keep(num(st.bytes / (ms * 1e-3) / 1e9))});
+    }
+    ipug_profile_sample &sm = samples[i];
+    std::memset(&sm, 0, sizeof sm);
+    sm.local_index = static_cast<uint32_t>(i);
+    sm.phase = static_cast<uint32_t>(i);
+    sm.kind = IPUG_STEP_COMPUTE;
+    sm.operation = keep("operation." + std::to_string(st.op_ids.empty() ? -1 : st.op_ids.front()));
+    sm.kernel = keep(st.label);
+    sm.metadata = m.data();
+    sm.metadata_count = static_cast<uint32_t>(m.size() / 2);
+    sm.start_cycle = cycles(t[i]);
+    sm.end_cycle = cycles(t[i + 1]);
+  }
+  const ipug_profile_tile tile = {physical_tile, samples.data(), n};
+  return ipug_profile_encode(1000000000ull, &tile, 1, buf, size, needed);
 }
 
 const char *ipug_session_plan(const ipug_session *s) { return s ? s->plan.c_str() : ""; }

@@ -45,6 +45,8 @@ _G_SIGS = {
     "ipug_session_run": (ctypes.c_int32, [_vp, _vp]),
     "ipug_session_profile": (ctypes.c_int32, [_vp, _vp, ctypes.c_char_p, ctypes.c_uint64,
                                               ctypes.POINTER(ctypes.c_uint64)]),
+    "ipug_session_profile_capnp": (ctypes.c_int32, [_vp, _vp, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint64,
+                                                    ctypes.POINTER(ctypes.c_uint64)]),
     "ipug_session_plan": (ctypes.c_char_p, [_vp]),
     "ipug_graph_plan": (ctypes.c_int32, [_vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
 }
@@ -225,6 +227,16 @@ class Session:
         buf = ctypes.create_string_buffer(int(need.value) + 64)
         self._call("ipug_session_profile", self._s, _stream(stream), buf, len(buf), ctypes.byref(need))
         return json.loads(buf.value.decode())
+
+    def profile_capnp(self, physical_tile: int = 0, stream=None) -> bytes:
+        """Run once with event timing and return the reference's Cap'n Proto
+        Profile message (decode with ipuc.profile.read)."""
+        need = ctypes.c_uint64(0)
+        glib().ipug_session_profile_capnp(self._s, _stream(stream), physical_tile, None, 0, ctypes.byref(need))
+        buf = ctypes.create_string_buffer(int(need.value) + 4096)  # labels may not change, timings can
+        self._call("ipug_session_profile_capnp", self._s, _stream(stream), physical_tile, buf, len(buf),
+                   ctypes.byref(need))
+        return buf.raw[:need.value]
 
     @property
     def plan(self) -> str:

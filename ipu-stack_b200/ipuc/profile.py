@@ -1,0 +1,333 @@
+"""Profile reports in the reference's Cap'n Proto format.
+
+The reference's profile is a `Profile` message (schemas/profile.capnp,
+schemas/profile_common.capnp) written and read by ProfileReport
+(crates/ipu-package/src/lib.rs:186-260) and queried by `ipu-profile query`
+(crates/ipu-profile/src/lib.rs:450-585).  On this backend a Session produces
+the same message from CUDA event timings (Session.profile_capnp, one tile per
+GPU, clockHz 1e9 so a cycle is a nanosecond); `write` encodes any report
+through the library's encoder (ipug_profile_encode) and `read` decodes one
+(any segment count, far pointers included) following the published Cap'n
+Proto encoding.  `merge` joins the one-tile reports of several GPUs, and
+`query` is the group-by summary of ipu-profile's query (count, cycles, ms per
+kernel, operation, kind, tile or phase).
+
+Data classes mirror the reference's Rust types: ProfileReport{clock_hz, tiles},
+TileProfile{physical_tile, samples}, CycleSample{step, start_cycle, end_cycle},
+ProfileStep{local_index, phase, epoch, operation, kind, kernel, metadata,
+exchange_activities, exchange_event_cycles}.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass, field
+
+from . import IpucError
+
+SCHEMA_VERSION = 5                      # crates/ipu-package/src/lib.rs:262
+STEP_KINDS = ("exchange", "compute", "synchronization", "idle")
+ACTIVITY_KINDS = ("send", "receive", "partnerBusy")
+
+
+class ProfileError(ValueError):
+    """A malformed or unsupported profile message (PackageError::Invalid / Capnp)."""
+
+
+@dataclass
+class ExchangeActivity:
+    kind: str
+    start_cycle: int
+    end_cycle: int
+
+
+@dataclass
+class ProfileStep:
+    local_index: int = 0
+    phase: int = 0
+    epoch: int = 0
+    operation: str = ""
+    kind: str = "compute"
+    kernel: str = ""
+    metadata: list = field(default_factory=list)          # [(name, value)]
+    exchange_activities: list = field(default_factory=list)
+    exchange_event_cycles: int = 0
+
+
+@dataclass
+class CycleSample:
+    step: ProfileStep
+    start_cycle: int
+    end_cycle: int
+
+
+@dataclass
+class TileProfile:
+    physical_tile: int
+    samples: list
+
+
+@dataclass
+class ProfileReport:
+    clock_hz: int
+    tiles: list
+
+
+# ---------------------------------------------------------------------------
+# Encoding (through the library)
+# ---------------------------------------------------------------------------
+
+class _Activity(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_uint32), ("start_cycle", ctypes.c_uint32), ("end_cycle", ctypes.c_uint32)]
+
+
+class _Sample(ctypes.Structure):
+    _fields_ = [("local_index", ctypes.c_uint32), ("phase", ctypes.c_uint32), ("epoch", ctypes.c_uint32),
+                ("kind", ctypes.c_uint32), ("operation", ctypes.c_char_p), ("kernel", ctypes.c_char_p),
+                ("metadata", ctypes.POINTER(ctypes.c_char_p)), ("metadata_count", ctypes.c_uint32),
+                ("activities", ctypes.POINTER(_Activity)), ("activity_count", ctypes.c_uint32),
+                ("exchange_event_cycles", ctypes.c_uint32), ("start_cycle", ctypes.c_uint32),
+                ("end_cycle", ctypes.c_uint32)]
+
+
+class _Tile(ctypes.Structure):
+    _fields_ = [("physical_tile", ctypes.c_uint32), ("samples", ctypes.POINTER(_Sample)),
+                ("sample_count", ctypes.c_uint64)]
+
+
+def _encoder():
+    from . import lib
+    fn = lib().ipug_profile_encode
+    fn.restype = ctypes.c_int32
+    fn.argtypes = [ctypes.c_uint64, ctypes.POINTER(_Tile), ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64,
+                   ctypes.POINTER(ctypes.c_uint64)]
+    return fn
+
+
+def write(report: ProfileReport) -> bytes:
+    """Encode `report` as a framed Profile message (ProfileReport::write)."""
+    keep = []   # ctypes objects that must outlive the call
+    tiles = (_Tile * max(1, len(report.tiles)))()
+    for t, tile in enumerate(report.tiles):
+        samples = (_Sample * max(1, len(tile.samples)))()
+        keep.append(samples)
+        for i, smp in enumerate(tile.samples):
+            st = smp.step
+            meta = (ctypes.c_char_p * max(1, 2 * len(st.metadata)))()
+            for j, (name, value) in enumerate(st.metadata):
+                meta[2 * j], meta[2 * j + 1] = name.encode(), value.encode()
+            acts = (_Activity * max(1, len(st.exchange_activities)))()
+            for j, a in enumerate(st.exchange_activities):
+                acts[j] = _Activity(ACTIVITY_KINDS.index(a.kind), a.start_cycle, a.end_cycle)
+            keep += [meta, acts]
+            samples[i] = _Sample(st.local_index, st.phase, st.epoch, STEP_KINDS.index(st.kind),
+                                 st.operation.encode(), st.kernel.encode(), meta, len(st.metadata), acts,
+                                 len(st.exchange_activities), st.exchange_event_cycles, smp.start_cycle,
+                                 smp.end_cycle)
+        tiles[t] = _Tile(tile.physical_tile, samples, len(tile.samples))
+    fn = _encoder()
+    need = ctypes.c_uint64(0)
+    fn(report.clock_hz, tiles, len(report.tiles), None, 0, ctypes.byref(need))
+    buf = ctypes.create_string_buffer(int(need.value))
+    rc = fn(report.clock_hz, tiles, len(report.tiles), buf, len(buf), ctypes.byref(need))
+    if rc != 0:
+        from . import lib
+        raise IpucError("ipug_profile_encode", rc, (lib().ipuc_last_error_string() or b"").decode())
+    return buf.raw[:need.value]
+
+
+# ---------------------------------------------------------------------------
+# Decoding (Cap'n Proto wire format, read side)
+# ---------------------------------------------------------------------------
+
+class _Message:
+    def __init__(self, data: bytes):
+        if len(data) < 8:
+            raise ProfileError("Cap'n Proto error: message shorter than its segment table")
+        count = struct.unpack_from("<I", data, 0)[0] + 1
+        head = 4 * (1 + count)
+        head += head % 8
+        if count > 512 or len(data) < head:
+            raise ProfileError("Cap'n Proto error: bad segment table")
+        sizes = struct.unpack_from(f"<{count}I", data, 4)
+        self.segments, off = [], head
+        for n in sizes:
+            if off + 8 * n > len(data):
+                raise ProfileError("Cap'n Proto error: segment runs past the end of the message")
+            self.segments.append(data[off:off + 8 * n])
+            off += 8 * n
+
+    def word(self, seg: int, idx: int) -> int:
+        s = self.segments[seg]
+        if not 0 <= idx < len(s) // 8:
+            raise ProfileError("Cap'n Proto error: pointer out of bounds")
+        return struct.unpack_from("<Q", s, 8 * idx)[0]
+
+    def resolve(self, seg: int, idx: int):
+        """Follow the pointer at (seg, idx): returns (tag word, seg, first word of
+        the target), or None for a null pointer."""
+        p = self.word(seg, idx)
+        if p == 0:
+            return None
+        if p & 3 == 2:                     # far pointer
+            double = (p >> 2) & 1
+            pad, tseg = (p >> 3) & 0x1FFFFFFF, p >> 32
+            if tseg >= len(self.segments):
+                raise ProfileError("Cap'n Proto error: far pointer to a missing segment")
+            if not double:
+                return self.resolve(tseg, pad)
+            land, tag = self.word(tseg, pad), self.word(tseg, pad + 1)
+            if land & 3 != 2:
+                raise ProfileError("Cap'n Proto error: bad double-far landing pad")
+            return tag, land >> 32, (land >> 3) & 0x1FFFFFFF
+        off = (p >> 2) & 0x3FFFFFFF
+        if off & 0x20000000:
+            off -= 0x40000000
+        return p, seg, idx + 1 + off
+
+
+class _Struct:
+    def __init__(self, msg: _Message, seg: int, at: int, dwords: int, pwords: int):
+        self.msg, self.seg, self.at, self.dwords, self.pwords = msg, seg, at, dwords, pwords
+
+    def _data(self, byte: int, fmt: str) -> int:
+        size = struct.calcsize(fmt)
+        if byte + size > 8 * self.dwords:   # field beyond an older, shorter struct: default 0
+            return 0
+        s = self.msg.segments[self.seg]
+        return struct.unpack_from("<" + fmt, s, 8 * self.at + byte)[0]
+
+    def u16(self, byte): return self._data(byte, "H")
+    def u32(self, byte): return self._data(byte, "I")
+    def u64(self, byte): return self._data(byte, "Q")
+
+    def _ptr(self, i: int):
+        if i >= self.pwords:
+            return None
+        return self.msg.resolve(self.seg, self.at + self.dwords + i)
+
+    def struct(self, i: int):
+        r = self._ptr(i)
+        if r is None:
+            return None
+        p, seg, at = r
+        if p & 3 != 0:
+            raise ProfileError("Cap'n Proto error: expected a struct pointer")
+        return _Struct(self.msg, seg, at, (p >> 32) & 0xFFFF, p >> 48)
+
+    def structs(self, i: int) -> list:
+        r = self._ptr(i)
+        if r is None:
+            return []
+        p, seg, at = r
+        if p & 3 != 1 or (p >> 32) & 7 != 7:
+            raise ProfileError("Cap'n Proto error: expected a list of structs")
+        tag = self.msg.word(seg, at)
+        n, dw, pw = (tag >> 2) & 0x3FFFFFFF, (tag >> 32) & 0xFFFF, tag >> 48
+        if n * (dw + pw) > p >> 35:
+            raise ProfileError("Cap'n Proto error: list elements exceed the list's word count")
+        return [_Struct(self.msg, seg, at + 1 + k * (dw + pw), dw, pw) for k in range(n)]
+
+    def text(self, i: int) -> str:
+        r = self._ptr(i)
+        if r is None:
+            return ""
+        p, seg, at = r
+        if p & 3 != 1 or (p >> 32) & 7 != 2:
+            raise ProfileError("Cap'n Proto error: expected Text")
+        n = p >> 35
+        raw = self.msg.segments[seg][8 * at:8 * at + n]
+        if len(raw) != n or n == 0 or raw[-1] != 0:
+            raise ProfileError("Cap'n Proto error: Text is not NUL-terminated")
+        try:
+            return raw[:-1].decode("utf-8")
+        except UnicodeDecodeError as e:
+            raise ProfileError(f"Cap'n Proto error: {e}") from None
+
+
+def _enum(names, v, what):
+    if v >= len(names):
+        raise ProfileError(f"Cap'n Proto error: enum value {v} not in {what}")
+    return names[v]
+
+
+def read(data: bytes) -> ProfileReport:
+    """Decode a framed Profile message (ProfileReport::read,
+    crates/ipu-package/src/lib.rs:225-259): schema versions 1-5 only."""
+    msg = _Message(bytes(data))
+    root = msg.resolve(0, 0)
+    if root is None or root[0] & 3 != 0:
+        raise ProfileError("Cap'n Proto error: root is not a struct")
+    p, seg, at = root
+    r = _Struct(msg, seg, at, (p >> 32) & 0xFFFF, p >> 48)
+    version = r.u32(0)
+    if not 1 <= version <= 5:
+        raise ProfileError(f"unsupported profile schema version {version}")
+    tiles = []
+    for t in r.structs(0):
+        samples = []
+        for s in t.structs(0):
+            st = s.struct(0)
+            step = ProfileStep()
+            if st is not None:
+                step = ProfileStep(
+                    local_index=st.u32(0), phase=st.u32(4), epoch=st.u32(8), operation=st.text(0),
+                    kind=_enum(STEP_KINDS, st.u16(12), "StepKind"), kernel=st.text(1),
+                    metadata=[(m.text(0), m.text(1)) for m in st.structs(2)],
+                    exchange_activities=[ExchangeActivity(_enum(ACTIVITY_KINDS, a.u16(0), "ExchangeActivityKind"),
+                                                          a.u32(4), a.u32(8)) for a in st.structs(3)],
+                    exchange_event_cycles=st.u32(16))
+            samples.append(CycleSample(step, s.u32(0), s.u32(4)))
+        tiles.append(TileProfile(t.u32(0), samples))
+    return ProfileReport(r.u64(8), tiles)
+
+
+# ---------------------------------------------------------------------------
+# Multi-GPU merge and query
+# ---------------------------------------------------------------------------
+
+def merge(reports) -> ProfileReport:
+    """One report with every tile of `reports` (e.g. one per GPU rank); all
+    must share clock_hz, as ipu-profile requires of the reports it joins
+    (crates/ipu-profile/src/lib.rs:215-224)."""
+    reports = list(reports)
+    if not reports:
+        raise ProfileError("no profile reports")
+    clock = reports[0].clock_hz
+    if any(r.clock_hz != clock for r in reports):
+        raise ProfileError("profile reports have different clock rates")
+    return ProfileReport(clock, [t for r in reports for t in r.tiles])
+
+
+def query(report: ProfileReport, group_by: str = "kernel", kind: str | None = None) -> list:
+    """Rows {name, samples, cycles, ms, tiles} grouped like ipu-profile's
+    query (GroupBy kind/kernel/operation/phase/tile,
+    crates/ipu-profile/src/lib.rs:632-668), sorted by cycles, largest first."""
+    groups = {}
+    for tile in report.tiles:
+        for smp in tile.samples:
+            st = smp.step
+            if kind is not None and st.kind != kind:
+                continue
+            if group_by == "kind":
+                name = st.kind
+            elif group_by == "kernel":
+                name = st.kernel or "(no kernel)"
+            elif group_by == "operation":
+                name = st.operation
+            elif group_by == "phase":
+                name = f"phase {st.phase}/{st.epoch}"
+            elif group_by == "tile":
+                name = f"tile {tile.physical_tile}"
+            else:
+                raise ValueError(f"unknown group_by {group_by!r}")
+            g = groups.setdefault(name, {"name": name, "samples": 0, "cycles": 0, "tiles": set()})
+            g["samples"] += 1
+            g["cycles"] += max(0, smp.end_cycle - smp.start_cycle)
+            g["tiles"].add(tile.physical_tile)
+    rows = sorted(groups.values(), key=lambda g: (-g["cycles"], g["name"]))
+    for g in rows:
+        g["ms"] = g["cycles"] * 1e3 / report.clock_hz if report.clock_hz else 0.0
+        g["tiles"] = sorted(g["tiles"])
+    return rows

@@ -73,6 +73,18 @@ def test_transformer_block_small():
     prof = s.profile()
     assert len(prof["steps"]) == plan.count("\n") and prof["total_ms"] > 0
     assert any("tflops" in st for st in prof["steps"])
+    # the same timings as the reference's Cap'n Proto Profile (one tile = this GPU)
+    from ipuc import profile as P
+    rep = P.read(s.profile_capnp(physical_tile=5))
+    assert rep.clock_hz == 1_000_000_000 and [t.physical_tile for t in rep.tiles] == [5]
+    samples = rep.tiles[0].samples
+    assert [smp.step.kernel for smp in samples] == [st["kernel"] for st in prof["steps"]]
+    assert all(smp.step.kind == "compute" and smp.step.operation.startswith("operation.") for smp in samples)
+    assert samples[0].start_cycle == 0
+    assert all(a.end_cycle <= b.start_cycle + 1 and a.start_cycle <= a.end_cycle for a, b in zip(samples, samples[1:]))
+    assert samples[-1].end_cycle > 0
+    top = P.query(rep, "kernel")[0]
+    assert top["samples"] >= 1 and top["ms"] > 0
 
 
 def test_attention_without_merge_keeps_split_heads():
