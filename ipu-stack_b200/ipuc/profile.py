@@ -331,3 +331,17 @@ def query(report: ProfileReport, group_by: str = "kernel", kind: str | None = No
         g["ms"] = g["cycles"] * 1e3 / report.clock_hz if report.clock_hz else 0.0
         g["tiles"] = sorted(g["tiles"])
     return rows
+
+
+def gather(data: bytes, group=None, dst: int = 0):
+    """Join the encoded one-tile reports of every rank of a torch.distributed
+    process group into one multi-tile report on rank `dst` (other ranks get
+    None): the multi-GPU counterpart of a whole-device profile, one tile per
+    GPU.  Collective: every rank of the group must call it."""
+    import torch.distributed as dist
+    rank = dist.get_rank(group)
+    parts = [None] * dist.get_world_size(group) if rank == dst else None
+    dist.gather_object(bytes(data), parts, dst=dst, group=group)
+    if rank != dst:
+        return None
+    return merge(read(p) for p in parts)

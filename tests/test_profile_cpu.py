@@ -164,3 +164,44 @@ def test_merge_and_query():
     assert P.query(m, "kernel", kind="idle") == []
     with pytest.raises(P.ProfileError):
         P.merge([r0, P.ProfileReport(2, [])])
+
+
+def _gather_worker(rank, world, port, out):
+    import os
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        step = P.ProfileStep(0, 0, 0, "operation.0", "compute", f"gemm_rank{rank}", [("device", str(rank))])
+        mine = P.ProfileReport(1_000_000_000, [P.TileProfile(rank, [P.CycleSample(step, 0, 1000 * (rank + 1))])])
+        merged = P.gather(P.write(mine))
+        if rank == 0:
+            out.put(P.write(merged))
+        else:
+            assert merged is None
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_across_gloo_ranks():
+    import socket
+
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    data = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rep = P.read(data)
+    assert [t.physical_tile for t in rep.tiles] == [0, 1]
+    assert [r["name"] for r in P.query(rep, "kernel")] == ["gemm_rank1", "gemm_rank0"]
