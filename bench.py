@@ -436,7 +436,7 @@ def measure_components(ipuc, torch, stream, hbm_gbs):
         gbs = 2 * n * 2 / (ms * 1e-3) / 1e9
         out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3)}
     del src, dst
-    # FP32 GEMM 4096^3 (3xTF32)
+    # FP32 GEMM 4096^3 (3xF16 split)
     try:
         m = n_ = k = 4096
         a32 = torch.rand((m, k), device="cuda") * 2 - 1

@@ -121,8 +121,11 @@ ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t
                                   int64_t stride_c, uint32_t flags, ipuc_stream stream);
 
 /* Replaces ipu_stack_gemm_f32_{init,accumulate}_* (device/gemm_f32_64_amp.S:
- * 129-385).  f32 in, f32 out, C (+)= A.B with three-pass TF32 splitting on the
- * tensor cores (hi.hi + hi.lo + lo.hi), accurate to an f32 tolerance.
+ * 129-385).  f32 in, f32 out, C (+)= A.B on the tensor cores with a
+ * three-pass f16 split (each row of A and column of B scaled by a power of
+ * two, then x = hi + lo in f16; hi.hi + hi.lo + lo.hi in fp32), accurate to
+ * an f32 tolerance relative to each row's and column's own magnitude.
+ * Non-finite inputs make the affected rows and columns NaN.
  * workspace: caller-provided device scratch of ipuc_gemm_f32_workspace_bytes()
  * bytes (the hi/lo split operands), 256-byte aligned.  Requirements:
  * 16-byte aligned pointers; k, n, lda and ldb multiples of 4 elements.
@@ -134,14 +137,16 @@ ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, int64_t m, i
 
 /* Allocation-free FP32 GEMM.  No counterpart in the reference: its tile
  * kernels never need scratch, while ipuc_gemm_f32 above takes a caller-provided
- * workspace for the TF32 hi/lo split planes.  This entry point is for callers
+ * workspace for the f16 hi/lo split planes.  This entry point is for callers
  * that cannot allocate device memory when they issue the GEMM (a plug-in whose
  * host framework owns the device allocator and forbids library allocations, a
  * host callback, or a real-time path whose memory budget is fixed up front):
  * the split planes live in a fixed 64 MiB file-scope device array of
  * libipuc.so instead.  Arguments, flags and results are exactly those
  * of ipuc_gemm_f32 without the workspace pair.
- *  - Limit: 2 * 4 * (m*k + k*n) <= 64 MiB (e.g. m = n = k = 2048); larger
+ *  - Limit: 4 * (m + n) * kp + 4 * m + 8 * n bytes (kp = k rounded up to 8,
+ *    each of the seven arrays rounded up to 256 bytes) <= 64 MiB (e.g.
+ *    m = n = k = 2880); larger
  *    shapes return IPUC_ERR_INVALID_ARGUMENT and launch nothing.
  *  - Allocates nothing: no cudaMalloc/cudaFree and no allocating library call.
  *    The array exists on every GPU that loads the library, until process exit.

@@ -41,7 +41,7 @@ enum : uint32_t {
   ERR_SITE_MMA = 2,
   ERR_SITE_EPILOGUE = 3,
   ERR_KERNEL_GEMM_F16 = 1u << 16,
-  ERR_KERNEL_GEMM_TF32 = 2u << 16,
+  ERR_KERNEL_GEMM_F32 = 2u << 16,
   ERR_KERNEL_ATTENTION = 3u << 16,
   ERR_KERNEL_SELFTEST = 4u << 16,
   ERR_KERNEL_LAYOUT = 5u << 16,

@@ -1,24 +1,31 @@
 // FP32 GEMM: the B200 counterpart of the reference's gemm_f32_64_amp tile
 // kernels (device/gemm_f32_64_amp.S:129-385, f32 multiply, f32 accumulate).
 //
-// fp32 accuracy on the tensor cores by three-pass TF32 splitting: every
-// operand x = hi + lo with hi = tf32(x) and lo = tf32(x - hi), and
+// fp32 accuracy on the tensor cores by a three-pass f16 split: every row of A
+// and column of B is scaled by a power of two (below), every scaled operand
+// x = hi + lo with hi = f16(x) and lo = f16(x - hi), and
 //   A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
 // (the dropped lo.lo term is ~2^-22 relative), accumulated in fp32 in TMEM.
-// The tensor core's fp32 accumulation loses precision over long chains of
-// MMAs into one accumulator, so each tile's K loop runs in chunks of 256:
-// every chunk accumulates into a fresh TMEM buffer (two, ping-ponged) and the
-// epilogue warps sum the chunk partials in fp32 registers.
-// A prepass kernel writes the hi/lo planes of A and of B (transposed to
-// K-major when B is row-major [k x n]) into the caller's workspace; the main
-// kernel is the same warp-specialised persistent tcgen05
-// pipeline as the FP16 GEMM (TMA producer / single-thread MMA issuer /
-// 4 epilogue warps, double-buffered 128x256 accumulators) issuing
-// kind::tf32 MMAs, three per 8-wide k step.
+// f16 carries the same 10 explicit mantissa bits as TF32, and kind::f16 MMAs
+// run at twice the kind::tf32 rate with half the operand bytes, so this split
+// matches the classic 3xTF32 one in accuracy at twice its MMA throughput.
+// Long chains of MMAs into one accumulator lose precision, so each tile's K
+// loop runs in chunks of 256: every chunk accumulates into a fresh TMEM
+// buffer (two, ping-ponged) and the epilogue warps sum the chunk partials in
+// fp32 registers.
+// Prepass kernels find the row maxima of A and the column maxima of B and
+// write the scaled hi/lo planes (B transposed to K-major when it is row-major
+// [k x n]) into the caller's workspace; the main kernel is the same
+// warp-specialised persistent tcgen05 pipeline as the FP16 GEMM (TMA producer
+// / single-thread MMA issuer / 8 epilogue warps, double-buffered 128x256
+// accumulators, CTA pairs when there is a wave of 256x256 tiles) issuing
+// three kind::f16 MMAs per K16 step, and its epilogue removes the scaling.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace ipuc {
@@ -26,56 +33,172 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 32, STAGES = 2;
-constexpr int A_BYTES = BM * BK * 4;  // 16 KB per plane
-constexpr int B_BYTES = BN * BK * 4;  // 32 KB per plane
+// A k-block is one 128-byte swizzle row of each plane (64 f16 elements); an
+// MMA k-step (K16) is 32 bytes of it.
+constexpr int BM = 128, BN = 256, BK = 64, BK_BYTES = BK * 2, STAGES = 2;
+constexpr int A_BYTES = BM * BK_BYTES;  // 16 KB per plane
+constexpr int B_BYTES = BN * BK_BYTES;  // 32 KB per plane
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // 96 KB
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int GROUP_M = 16;
-constexpr int KC = 8;            // k-blocks (of 32) per TMEM accumulation chunk
+constexpr int CHUNK_K = 256;     // K per TMEM accumulation chunk
+constexpr int KC = CHUNK_K / BK; // k-blocks per chunk
 constexpr int EPI_THREADS = 256; // 8 epilogue warps
 constexpr int NUM_THREADS = 64 + EPI_THREADS;
 
-// Round to TF32 (10 explicit mantissa bits), nearest, ties away from zero.
-__device__ __forceinline__ float to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+// ---- 3xF16 split with power-of-two row/column scaling ----
+// f16 has TF32's 10 explicit mantissa bits but only a 5-bit exponent, so each
+// row of A and each column of B is first scaled by an exact power of two 2^e
+// that puts its largest magnitude in [2^14, 2^15): then hi = f16(x 2^e) and
+// lo = f16(x 2^e - hi) carry 22 bits for every element within 2^17 of the
+// row's maximum (smaller ones keep an absolute error below 2^-39 of it), and
+// the MMA products of the scaled planes equal the TF32 split's to the bit
+// budget.  The epilogue multiplies C by 2^-(e_row + e_col).  Maxima are kept
+// as float bits (non-negative floats order like their bit patterns).
+
+// e such that mx * 2^e lies in [2^14, 2^15); 0 for zero, inf and NaN rows;
+// at most 126 so that 2^e and 2^-e are normal floats.
+__host__ __device__ __forceinline__ int split_exponent(uint32_t max_bits) {
+  const uint32_t f = max_bits >> 23;
+  if (max_bits == 0 || f >= 255) return 0;
+#ifdef __CUDA_ARCH__
+  const int lz = __clz(max_bits);
+#else
+  const int lz = __builtin_clz(max_bits);
+#endif
+  const int ex = f ? (int)f - 127 : (31 - lz) - 149;  // floor(log2(mx))
+  const int e = 14 - ex;
+  return e < 126 ? e : 126;
 }
 
-// hi/lo planes of a row-major [rows x cols] matrix with leading dimension ld
-// into dense [rows x cols] planes.
-__global__ void __launch_bounds__(256) split_tf32_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
-                                                         int64_t ld, float *__restrict__ hi, float *__restrict__ lo) {
-  const int64_t total4 = rows * cols / 4;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
-    const int64_t e = i * 4, r = e / cols, c = e % cols;
-    const float4 x = *reinterpret_cast<const float4 *>(src + r * ld + c);
-    float4 h, l;
-    h.x = to_tf32(x.x); l.x = to_tf32(x.x - h.x);
-    h.y = to_tf32(x.y); l.y = to_tf32(x.y - h.y);
-    h.z = to_tf32(x.z); l.z = to_tf32(x.z - h.z);
-    h.w = to_tf32(x.w); l.w = to_tf32(x.w - h.w);
-    reinterpret_cast<float4 *>(hi)[i] = h;
-    reinterpret_cast<float4 *>(lo)[i] = l;
+__device__ __forceinline__ float pow2(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+
+__device__ __forceinline__ void split_f16(float x, float scale, __half &h, __half &l) {
+  const float xs = x * scale;
+  h = __float2half_rn(xs);
+  l = __float2half_rn(xs - __half2float(h));
+}
+
+// Largest |x| of every column of a row-major [rows x cols] matrix into out
+// (zeroed by the caller).  A CTA covers 128 columns x COLMAX_ROWS rows: 8 row
+// lanes of 32 threads, each thread 4 columns with four 16-byte loads in
+// flight; the 8 row lanes merge through shared memory and one atomicMax per
+// column and CTA (on the float bits) merges the CTAs.
+constexpr int COLMAX_ROWS = 128;
+__global__ void __launch_bounds__(256) col_absmax_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                         int64_t ld, uint32_t *__restrict__ out) {
+  __shared__ float4 part[8][32];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t col_tiles = (cols + 127) / 128, bands = (rows + COLMAX_ROWS - 1) / COLMAX_ROWS;
+  for (int64_t t = blockIdx.x; t < col_tiles * bands; t += gridDim.x) {
+    const int64_t c = (t % col_tiles) * 128 + 4 * tx;
+    const int64_t r0 = (t / col_tiles) * COLMAX_ROWS, r1 = min(rows, r0 + COLMAX_ROWS);
+    float4 mx = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (c < cols) {
+      for (int64_t r = r0 + ty; r < r1; r += 32) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = r + 8 * u < r1 ? __ldg(reinterpret_cast<const float4 *>(src + (r + 8 * u) * ld + c))
+                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          mx.x = fmaxf(mx.x, fabsf(v[u].x)); mx.y = fmaxf(mx.y, fabsf(v[u].y));
+          mx.z = fmaxf(mx.z, fabsf(v[u].z)); mx.w = fmaxf(mx.w, fabsf(v[u].w));
+        }
+      }
+    }
+    __syncthreads();
+    part[ty][tx] = mx;
+    __syncthreads();
+    if (ty == 0 && c < cols) {
+#pragma unroll
+      for (int y = 1; y < 8; ++y) {
+        const float4 o = part[y][tx];
+        mx.x = fmaxf(mx.x, o.x); mx.y = fmaxf(mx.y, o.y); mx.z = fmaxf(mx.z, o.z); mx.w = fmaxf(mx.w, o.w);
+      }
+      atomicMax(out + c, __float_as_uint(mx.x));
+      atomicMax(out + c + 1, __float_as_uint(mx.y));
+      atomicMax(out + c + 2, __float_as_uint(mx.z));
+      atomicMax(out + c + 3, __float_as_uint(mx.w));
+    }
   }
 }
 
-// hi/lo planes of B^T: B is row-major [rows x cols] (ld); the planes are dense
-// [cols x rows], so the MMA reads B K-major.  64x64 tiles through shared memory,
-// 16-byte loads and stores (each thread moves 16 elements each way) so that
-// enough bytes are in flight per SM to run near HBM bandwidth; the padded tile
-// row (65 floats) keeps the column reads conflict-free.  Vector accesses need
-// rows, cols and ld to be multiples of 4 (the gemm_f32 entry requires that);
-// ragged 64x64 tiles fall back to scalar accesses.
-__global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float *__restrict__ src, int64_t rows,
-                                                                   int64_t cols, int64_t ld, float *__restrict__ hi,
-                                                                   float *__restrict__ lo) {
+// Row exponents and f16 hi/lo planes [rows x ldp] of a row-major [rows x
+// cols] matrix with one read of the matrix: one CTA per row holds the row in
+// registers (ROW_CACHE float4 per thread: rows up to 4096 floats; longer rows
+// re-read their remainder, from L2), reduces the row's largest |x| through
+// shared memory, stores the row's split exponent to rexp for the epilogue and
+// writes the row scaled and split.  Pad columns [cols, ldp) are zero.  cols
+// and ld are multiples of 4.
+constexpr int ROW_CACHE = 4;
+__global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                             int64_t ld, int32_t *__restrict__ rexp, int64_t ldp,
+                                                             __half *__restrict__ hi, __half *__restrict__ lo) {
+  __shared__ float red[8];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t q = cols / 4, qp = ldp / 4;
+  const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  auto amax4 = [](float m, float4 x) {
+    return fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+  };
+  auto put = [&](int64_t r, int64_t c, float4 x, float scale) {
+    __half h[4], l[4];
+    split_f16(x.x, scale, h[0], l[0]);
+    split_f16(x.y, scale, h[1], l[1]);
+    split_f16(x.z, scale, h[2], l[2]);
+    split_f16(x.w, scale, h[3], l[3]);
+    *reinterpret_cast<uint2 *>(hi + r * ldp + 4 * c) = *reinterpret_cast<const uint2 *>(h);
+    *reinterpret_cast<uint2 *>(lo + r * ldp + 4 * c) = *reinterpret_cast<const uint2 *>(l);
+  };
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float4 *row = reinterpret_cast<const float4 *>(src + r * ld);
+    float4 v[ROW_CACHE];
+    float mx = 0.0f;
+#pragma unroll
+    for (int u = 0; u < ROW_CACHE; ++u) {
+      const int64_t c = tid + u * 256;
+      v[u] = c < q ? row[c] : zero;
+      mx = amax4(mx, v[u]);
+    }
+    for (int64_t c = tid + ROW_CACHE * 256; c < q; c += 256) mx = amax4(mx, row[c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[wid] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();  // red is rewritten for the next row
+    const int e = split_exponent(__float_as_uint(mx));
+    if (tid == 0) rexp[r] = e;
+    const float scale = pow2(e);
+#pragma unroll
+    for (int u = 0; u < ROW_CACHE; ++u) {
+      const int64_t c = tid + u * 256;
+      if (c < qp) put(r, c, v[u], scale);
+    }
+    for (int64_t c = tid + ROW_CACHE * 256; c < qp; c += 256) put(r, c, c < q ? row[c] : zero, scale);
+  }
+}
+
+// f16 hi/lo planes of B^T: B row-major [rows x cols] (ld) -> planes
+// [cols x ldp] (K-major), source column c scaled by 2^split_exponent(cmax[c]);
+// the tiles of the first row band also store the column exponents to cexp.
+// 64x64 tiles through shared memory (16-byte loads; the padded tile row of 65
+// floats keeps the column reads conflict-free); pad elements [rows, ldp) of
+// each plane row are zero.  Full 64x64 tiles need rows, cols and ld multiples
+// of 4 (the gemm_f32 entry requires that); ragged tiles use scalar loads.
+__global__ void __launch_bounds__(256) split_f16_transpose_kernel(const float *__restrict__ src, int64_t rows,
+                                                                  int64_t cols, int64_t ld,
+                                                                  const uint32_t *__restrict__ cmax, int64_t ldp,
+                                                                  __half *__restrict__ hi, __half *__restrict__ lo,
+                                                                  int32_t *__restrict__ cexp) {
   __shared__ float tile[64][65];
-  const int64_t tr = (rows + 63) / 64, tc = (cols + 63) / 64;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads, 4 consecutive elements each
+  const int64_t tr = (ldp + 63) / 64, tc = (cols + 63) / 64;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   for (int64_t t = blockIdx.x; t < tr * tc; t += gridDim.x) {
     const int64_t r0 = (t / tc) * 64, c0 = (t % tc) * 64;
     const bool full = r0 + 64 <= rows && c0 + 64 <= cols;
@@ -101,26 +224,17 @@ __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float *
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int oc = ty + 16 * i, orr = tx * 4;  // output row = source column c0 + oc
+      const int oc = ty + 16 * i, orr = tx * 4;  // plane row = source column c0 + oc
       const int64_t c = c0 + oc, r = r0 + orr;
-      float x[4], h[4], l[4];
+      if (c >= cols || r >= ldp) continue;
+      const int ce = split_exponent(cmax[c]);
+      if (r0 == 0 && tx == 0) cexp[c] = ce;
+      const float scale = pow2(ce);
+      __half h[4], l[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        x[e] = tile[orr + e][oc];
-        h[e] = to_tf32(x[e]);
-        l[e] = to_tf32(x[e] - h[e]);
-      }
-      if (full) {
-        *reinterpret_cast<float4 *>(hi + c * rows + r) = make_float4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<float4 *>(lo + c * rows + r) = make_float4(l[0], l[1], l[2], l[3]);
-      } else if (c < cols) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (r + e < rows) {
-            hi[c * rows + r + e] = h[e];
-            lo[c * rows + r + e] = l[e];
-          }
-      }
+      for (int e = 0; e < 4; ++e) split_f16(tile[orr + e][oc], scale, h[e], l[e]);
+      *reinterpret_cast<uint2 *>(hi + c * ldp + r) = *reinterpret_cast<const uint2 *>(h);
+      *reinterpret_cast<uint2 *>(lo + c * ldp + r) = *reinterpret_cast<const uint2 *>(l);
     }
   }
 }
@@ -133,7 +247,16 @@ struct Gemm32Params {
   int64_t num_tiles;
   uint32_t flags;
   uint32_t *err;
+  const int32_t *ea, *eb;  // split exponents of the rows of A and the columns of B
 };
+
+// C element scale 2^-(e_row + e_col) of the 3xF16 split, exact unless C itself
+// over- or underflows.
+__device__ __forceinline__ float unscale(float v, int e_row, int e_col) {
+  const int e = e_row + e_col;
+  if (e >= -126 && e <= 126) return v * pow2(-e);
+  return (v * pow2(-e_row)) * pow2(-e_col);
+}
 
 __device__ __forceinline__ void tile_coords(const Gemm32Params &p, int64_t t, int &mt, int &nt) {
   const int64_t in_group = (int64_t)GROUP_M * p.tiles_n;
@@ -146,7 +269,7 @@ __device__ __forceinline__ void tile_coords(const Gemm32Params &p, int64_t t, in
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+    gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                        const Gemm32Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -205,13 +328,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) {
-        record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_PRODUCER);
+        record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_PRODUCER);
         *abort_flag = 1;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BM, BN, /*tf32*/ 2, false, false);
+      constexpr uint32_t idesc = make_idesc(BM, BN, /*f16*/ 0, false, false);
       uint32_t it = 0, g = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
@@ -235,15 +358,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t ah = smem_u32(smem + s * STAGE_BYTES), al = ah + A_BYTES;
             const uint32_t bh = ah + 2 * A_BYTES, bl = bh + B_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK / 8; ++k) {
+            for (int k = 0; k < BK_BYTES / 32; ++k) {  // K16 steps of 32 bytes
               const uint64_t dah = make_smem_desc(ah + k * 32, 16, 1024, kSwizzle128B);
               const uint64_t dal = make_smem_desc(al + k * 32, 16, 1024, kSwizzle128B);
               const uint64_t dbh = make_smem_desc(bh + k * 32, 16, 1024, kSwizzle128B);
               const uint64_t dbl = make_smem_desc(bl + k * 32, 16, 1024, kSwizzle128B);
               // Small terms first, then the dominant hi.hi product.
-              mma_tf32_ss(d_tmem, dal, dbh, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
-              mma_tf32_ss(d_tmem, dah, dbl, idesc, 1u);
-              mma_tf32_ss(d_tmem, dah, dbh, idesc, 1u);
+              mma_f16_ss(d_tmem, dal, dbh, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
+              mma_f16_ss(d_tmem, dah, dbl, idesc, 1u);
+              mma_f16_ss(d_tmem, dah, dbh, idesc, 1u);
             }
             mma_commit(&empty[s]);
           }
@@ -252,7 +375,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) {
-        record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_MMA);
+        record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_MMA);
         *abort_flag = 1;
       }
     }
@@ -294,12 +417,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t row = (int64_t)mt * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
+        const int er = p.ea[row];
         float *cp = p.c + row * p.ldc + col_base;
         if (vec_ok && col_base + BN / 2 <= p.n) {
           float4 *c4 = reinterpret_cast<float4 *>(cp);
 #pragma unroll
           for (int j = 0; j < BN / 8; ++j) {
             float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+            {
+              const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col_base) + j);
+              v.x = unscale(v.x, er, ec.x);
+              v.y = unscale(v.y, er, ec.y);
+              v.z = unscale(v.z, er, ec.z);
+              v.w = unscale(v.w, er, ec.w);
+            }
             if (accumulate) {
               const float4 o = c4[j];
               v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
@@ -311,6 +442,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int j = 0; j < BN / 2; ++j) {
             if (col_base + j < p.n) {
               float x = acc[j];
+              x = unscale(x, er, p.eb[col_base + j]);
               if (accumulate) x += cp[j];
               cp[j] = x;
             }
@@ -319,7 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (!ok) {
-      record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_EPILOGUE);
+      record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_EPILOGUE);
       *abort_flag = 1;
     }
   }
@@ -342,7 +474,7 @@ constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr int PAIR_BM = 2 * BM;
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-    gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+    gemm_f16x3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                             const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                             const Gemm32Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -404,13 +536,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) {
-        record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_PRODUCER);
+        record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_PRODUCER);
         *abort_flag = 1;
       }
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*tf32*/ 2, false, false);
+      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*f16*/ 0, false, false);
       // Descriptors built once; stages and k-steps add offsets in 16-byte units.
       const uint64_t d0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       uint32_t it = 0, g = 0;
@@ -438,12 +570,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const uint64_t dbh = dah + (uint64_t)((2 * A_BYTES) >> 4);
             const uint64_t dbl = dah + (uint64_t)((3 * A_BYTES) >> 4);
 #pragma unroll
-            for (int k = 0; k < BK / 8; ++k) {
+            for (int k = 0; k < BK_BYTES / 32; ++k) {  // K16 steps of 32 bytes
               const uint64_t o = (uint64_t)((k * 32) >> 4);
               // Small terms first, then the dominant hi.hi product.
-              mma_tf32_ss_pair(d_tmem, dal + o, dbh + o, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
-              mma_tf32_ss_pair(d_tmem, dah + o, dbl + o, idesc, 1u);
-              mma_tf32_ss_pair(d_tmem, dah + o, dbh + o, idesc, 1u);
+              mma_f16_ss_pair(d_tmem, dal + o, dbh + o, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
+              mma_f16_ss_pair(d_tmem, dah + o, dbl + o, idesc, 1u);
+              mma_f16_ss_pair(d_tmem, dah + o, dbh + o, idesc, 1u);
             }
             mma_commit_pair(&empty[s], 0x3);
           }
@@ -452,7 +584,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) {
-        record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_MMA);
+        record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_MMA);
         *abort_flag = 1;
       }
     }
@@ -493,12 +625,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
+        const int er = p.ea[row];
         float *cp = p.c + row * p.ldc + col_base;
         if (vec_ok && col_base + BN / 2 <= p.n) {
           float4 *c4 = reinterpret_cast<float4 *>(cp);
 #pragma unroll
           for (int j = 0; j < BN / 8; ++j) {
             float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+            {
+              const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col_base) + j);
+              v.x = unscale(v.x, er, ec.x);
+              v.y = unscale(v.y, er, ec.y);
+              v.z = unscale(v.z, er, ec.z);
+              v.w = unscale(v.w, er, ec.w);
+            }
             if (accumulate) {
               const float4 o = c4[j];
               v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
@@ -510,6 +650,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           for (int j = 0; j < BN / 2; ++j) {
             if (col_base + j < p.n) {
               float x = acc[j];
+              x = unscale(x, er, p.eb[col_base + j]);
               if (accumulate) x += cp[j];
               cp[j] = x;
             }
@@ -518,7 +659,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (!ok) {
-      record_device_error(p.err, ERR_KERNEL_GEMM_TF32 | ERR_SITE_EPILOGUE);
+      record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_EPILOGUE);
       *abort_flag = 1;
     }
   }
@@ -533,12 +674,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 inline uint64_t round256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
+// Workspace: A_hi, A_lo [m x kp] and B_hi, B_lo [n x kp] f16 (kp = k rounded
+// up to 8, so that plane rows are 16-byte multiples for TMA), then the split
+// exponents of A's rows [m] and B's columns [n] (int32) and B's column maxima
+// [n] (u32 float bits, row-major B only), each 256-byte aligned.
+int64_t f16_pitch(int64_t k) { return (k + 7) & ~int64_t(7); }
+
+ipuc_status launch_main(const CUtensorMap &tah, const CUtensorMap &tal, void *bh, void *bl, int64_t m, int64_t n,
+                        int64_t k, int64_t ldp, Gemm32Params &p, cudaStream_t stream) {
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  ipuc_status st;
+  p.tiles_n = (int32_t)((n + BN - 1) / BN);
+  p.k_blocks = (int32_t)((k + BK - 1) / BK);
+  const int sms = sm_count();
+  const int64_t pair_tiles = ((m + PAIR_BM - 1) / PAIR_BM) * (int64_t)p.tiles_n;
+  if (m > BM && sms >= 2 && pair_tiles >= sms / 2) {
+    // CTA pairs (at least one full wave of 256x256 tiles; below that the
+    // single-CTA kernel spreads the work over more SMs): A boxes of 128 rows
+    // per CTA, B boxes of 128 rows (half of BN).
+    CUtensorMap pbh, pbl;
+    if ((st = make_map_3d(&pbh, dt, 2, bh, k, n, 1, ldp, 0, BK, BN / 2)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&pbl, dt, 2, bl, k, n, 1, ldp, 0, BK, BN / 2)) != IPUC_OK) return st;
+    p.tiles_m = (int32_t)((m + PAIR_BM - 1) / PAIR_BM);
+    p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
+    const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    IPUC_CUDA(cudaFuncSetAttribute(gemm_f16x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+    gemm_f16x3_pair_kernel<<<(unsigned)(2 * pairs), NUM_THREADS, P_SMEM_BYTES, stream>>>(tah, tal, pbh, pbl, p);
+    return check_launch("gemm_f16x3_pair_kernel");
+  }
+  CUtensorMap tbh, tbl;
+  if ((st = make_map_3d(&tbh, dt, 2, bh, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
+  if ((st = make_map_3d(&tbl, dt, 2, bl, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
+  p.tiles_m = (int32_t)((m + BM - 1) / BM);
+  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
+  const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
+  IPUC_CUDA(cudaFuncSetAttribute(gemm_f16x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  gemm_f16x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tah, tal, tbh, tbl, p);
+  return check_launch("gemm_f16x3_kernel");
+}
+
 }  // namespace
 
-// Workspace: A_hi, A_lo [m x k] and B_hi, B_lo (B's shape), dense fp32.
 uint64_t gemm_f32_workspace(int64_t m, int64_t n, int64_t k) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
-  return 2 * round256((uint64_t)m * k * 4) + 2 * round256((uint64_t)k * n * 4);
+  const uint64_t kp = (uint64_t)f16_pitch(k);
+  return 2 * round256((uint64_t)m * kp * 2) + 2 * round256((uint64_t)n * kp * 2) + round256((uint64_t)m * 4) +
+         2 * round256((uint64_t)n * 4);
 }
 
 ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda,
@@ -561,64 +742,48 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
                  "gemm_f32: workspace smaller than ipuc_gemm_f32_workspace_bytes()");
   IPUC_CHECK_ALIGN(aligned(workspace, 256), "gemm_f32: workspace must be 256-byte aligned");
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  float *ah = reinterpret_cast<float *>(ws);
-  float *al = reinterpret_cast<float *>(ws + round256((uint64_t)m * k * 4));
-  float *bh = reinterpret_cast<float *>(ws + 2 * round256((uint64_t)m * k * 4));
-  float *bl = reinterpret_cast<float *>(ws + 2 * round256((uint64_t)m * k * 4) + round256((uint64_t)k * n * 4));
-  const int64_t brows = bt ? n : k, bcols = bt ? k : n;
   const int cap = sm_count() * 8;
-  auto grid_of = [&](int64_t elems) {
-    int64_t g = (elems / 4 + 255) / 256;
-    return (unsigned)(g < cap ? (g < 1 ? 1 : g) : cap);
-  };
-  split_tf32_kernel<<<grid_of(m * k), 256, 0, stream>>>(a, m, k, lda, ah, al);
-  if (bt) {
-    split_tf32_kernel<<<grid_of(brows * bcols), 256, 0, stream>>>(b, brows, bcols, ldb, bh, bl);
-  } else {
-    const int64_t tiles = ((k + 63) / 64) * ((n + 63) / 64);
-    const unsigned g = (unsigned)(tiles < cap ? tiles : cap);
-    split_tf32_transpose_kernel<<<g, 256, 0, stream>>>(b, k, n, ldb, bh, bl);
-  }
-  ipuc_status st = check_launch("split_tf32_kernel");
-  if (st != IPUC_OK) return st;
 
-  CUtensorMap tah, tal, tbh, tbl;
-  const auto f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  if ((st = make_map_3d(&tah, f32, 4, ah, k, m, 1, k, 0, BK, BM)) != IPUC_OK) return st;
-  if ((st = make_map_3d(&tal, f32, 4, al, k, m, 1, k, 0, BK, BM)) != IPUC_OK) return st;
-  // Both B layouts arrive as dense K-major [n x k] planes.
-  if ((st = make_map_3d(&tbh, f32, 4, bh, k, n, 1, k, 0, BK, BN)) != IPUC_OK) return st;
-  if ((st = make_map_3d(&tbl, f32, 4, bl, k, n, 1, k, 0, BK, BN)) != IPUC_OK) return st;
   Gemm32Params p;
   p.c = c;
   p.m = m; p.n = n; p.k = k;
   p.ldc = ldc;
-  p.tiles_n = (int32_t)((n + BN - 1) / BN);
-  p.k_blocks = (int32_t)((k + BK - 1) / BK);
   p.flags = flags;
   p.err = device_error_word();
-  const int sms = sm_count();
-  const int64_t pair_tiles = ((m + PAIR_BM - 1) / PAIR_BM) * (int64_t)p.tiles_n;
-  if (m > BM && sms >= 2 && pair_tiles >= sms / 2) {
-    // CTA pairs (at least one full wave of 256x256 tiles; below that the
-    // single-CTA kernel spreads the work over more SMs): A boxes of 128 rows
-    // per CTA, B boxes of 128 rows (half of BN).
-    CUtensorMap pbh, pbl;
-    if ((st = make_map_3d(&pbh, f32, 4, bh, k, n, 1, k, 0, BK, BN / 2)) != IPUC_OK) return st;
-    if ((st = make_map_3d(&pbl, f32, 4, bl, k, n, 1, k, 0, BK, BN / 2)) != IPUC_OK) return st;
-    p.tiles_m = (int32_t)((m + PAIR_BM - 1) / PAIR_BM);
-    p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
-    const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
-    IPUC_CUDA(cudaFuncSetAttribute(gemm_tf32x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-    gemm_tf32x3_pair_kernel<<<(unsigned)(2 * pairs), NUM_THREADS, P_SMEM_BYTES, stream>>>(tah, tal, pbh, pbl, p);
-    return check_launch("gemm_tf32x3_pair_kernel");
+  p.ea = p.eb = nullptr;
+  ipuc_status st;
+  CUtensorMap tah, tal;
+
+  {
+    const int64_t kp = f16_pitch(k);
+    __half *ah = reinterpret_cast<__half *>(ws);
+    __half *al = reinterpret_cast<__half *>(ws + round256((uint64_t)m * kp * 2));
+    uint8_t *bbase = ws + 2 * round256((uint64_t)m * kp * 2);
+    __half *bh = reinterpret_cast<__half *>(bbase);
+    __half *bl = reinterpret_cast<__half *>(bbase + round256((uint64_t)n * kp * 2));
+    uint8_t *mbase = bbase + 2 * round256((uint64_t)n * kp * 2);
+    int32_t *ea = reinterpret_cast<int32_t *>(mbase);
+    int32_t *eb = reinterpret_cast<int32_t *>(mbase + round256((uint64_t)m * 4));
+    uint32_t *bmax = reinterpret_cast<uint32_t *>(mbase + round256((uint64_t)m * 4) + round256((uint64_t)n * 4));
+    split_f16_rows_kernel<<<(unsigned)(m < cap ? m : cap), 256, 0, stream>>>(a, m, k, lda, ea, kp, ah, al);
+    if (bt) {
+      split_f16_rows_kernel<<<(unsigned)(n < cap ? n : cap), 256, 0, stream>>>(b, n, k, ldb, eb, kp, bh, bl);
+    } else {
+      IPUC_CUDA(cudaMemsetAsync(bmax, 0, (size_t)n * 4, stream));
+      const int64_t col_ctas = ((n + 127) / 128) * ((k + COLMAX_ROWS - 1) / COLMAX_ROWS);
+      col_absmax_kernel<<<(unsigned)(col_ctas < cap ? col_ctas : cap), 256, 0, stream>>>(b, k, n, ldb, bmax);
+      const int64_t tiles = ((kp + 63) / 64) * ((n + 63) / 64);
+      split_f16_transpose_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(b, k, n, ldb, bmax, kp,
+                                                                                            bh, bl, eb);
+    }
+    if ((st = check_launch("gemm_f32 split (3xF16)")) != IPUC_OK) return st;
+    const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if ((st = make_map_3d(&tah, f16, 2, ah, k, m, 1, kp, 0, BK, BM)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&tal, f16, 2, al, k, m, 1, kp, 0, BK, BM)) != IPUC_OK) return st;
+    p.ea = ea;
+    p.eb = eb;
+    return launch_main(tah, tal, bh, bl, m, n, k, kp, p, stream);
   }
-  p.tiles_m = (int32_t)((m + BM - 1) / BM);
-  p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
-  const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
-  IPUC_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tah, tal, tbh, tbl, p);
-  return check_launch("gemm_tf32x3_kernel");
 }
 
 }  // namespace ipuc
@@ -642,7 +807,7 @@ extern "C" ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, i
 // FP32 GEMM: a plug-in loaded into a host framework that owns the device
 // allocator and forbids cudaMalloc from library code, code running in a host
 // callback, or a real-time path whose memory budget is fixed up front.  They get ipuc_gemm_f32_noalloc: the same kernels, with the
-// hi/lo TF32 split planes placed in a fixed file-scope device array instead
+// hi/lo f16 split planes placed in a fixed file-scope device array instead
 // of a caller-provided workspace.
 //
 // The array is a device symbol, so on the host its name is only a stand-in:
@@ -686,10 +851,10 @@ extern "C" ipuc_status ipuc_gemm_f32_noalloc(float *c, const float *a, const flo
                                              ipuc_stream stream) {
   const uint64_t need = ipuc::gemm_f32_workspace(m, n, k);
   if (need > ipuc::kNoAllocScratchBytes) {
-    char buf[200];
+    char buf[320];
     snprintf(buf, sizeof(buf),
              "gemm_f32_noalloc: m=%lld n=%lld k=%lld needs %llu scratch bytes, above the fixed %llu-byte array "
-             "(2*4*(m*k + k*n) <= 64 MiB); use ipuc_gemm_f32 with a workspace",
+             "(about 4*(m + n)*k <= 64 MiB); use ipuc_gemm_f32 with a workspace",
              (long long)m, (long long)n, (long long)k, (unsigned long long)need,
              (unsigned long long)ipuc::kNoAllocScratchBytes);
     return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, buf);

@@ -1,4 +1,4 @@
-"""Parity of the three-pass TF32 FP32 GEMM (gemm_f32_64_amp replacement)
+"""Parity of the three-pass f16-split FP32 GEMM (gemm_f32_64_amp replacement)
 against the oracle's f32 SGEMM (diagnostic.rs:581-654).  BASELINE tolerance:
 rel-L2 <= 1e-5."""
 import numpy as np
@@ -69,3 +69,54 @@ def test_gemm_f32_workspace_checked():
     with pytest.raises(ipuc.IpucError) as e:
         ipuc.gemm_f32(a, a, a, 64, 64, 64, small)
     assert e.value.status == ipuc.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_f32_row_and_column_scales(bt):
+    """The f16 split scales every row of A and column of B by its own power of
+    two, so rows and columns spread over 1e-36 .. 1e35 keep fp32 accuracy
+    relative to their own size: C_ij / (sA_i sB_j) against fp64 within rel-L2
+    1e-5 (scales chosen so that C itself stays inside the fp32 range; the
+    combined exponent still leaves the single-multiply range, which takes the
+    two-step unscale).  All-zero rows and columns give exact zeros."""
+    m, n, k = 384, 520, 300
+    rng = np.random.default_rng(41)
+    sa = 10.0 ** rng.uniform(-28, 27, m)
+    sb = 10.0 ** rng.uniform(-8, 8, n)
+    a0 = seeded_uniform(42, (m, k)).astype(np.float64)
+    b0 = seeded_uniform(43, (k, n)).astype(np.float64)
+    a0[5] = 0.0
+    b0[:, 7] = 0.0
+    a = (a0 * sa[:, None]).astype(np.float32)
+    b = (b0 * sb[None, :]).astype(np.float32)
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    bd = np.ascontiguousarray(b.T) if bt else b
+    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    ws = torch.empty(ipuc.gemm_f32_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    ipuc.gemm_f32(c, dev_f32(a), dev_f32(bd), m, n, k, ws, ipuc.GEMM_B_TRANSPOSED if bt else 0)
+    got = host_f32(c).astype(np.float64)
+    assert np.isfinite(got).all()
+    scale = sa[:, None] * sb[None, :]
+    assert rel_l2(got / scale, ref / scale) <= 1e-5
+    assert (got[5] == 0).all() and (got[:, 7] == 0).all()
+
+
+def test_gemm_f32_tiny_and_huge_magnitudes():
+    """Rows near the fp32 limits (subnormal and 1e38 maxima) stay accurate
+    relative to their own maximum."""
+    m, n, k = 256, 256, 128
+    a0 = seeded_uniform(51, (m, k)).astype(np.float64)
+    b = seeded_uniform(52, (k, n))
+    a0[0] *= 1e-40                       # subnormal fp32 row
+    a0[1] *= 1e-36
+    a0[2] *= 1e37 / np.abs(a0[2]).max()  # largest element 1e37 (C stays below the fp32 limit)
+    a = a0.astype(np.float32)
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    ws = torch.empty(ipuc.gemm_f32_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    ipuc.gemm_f32(c, dev_f32(a), dev_f32(b), m, n, k, ws)
+    got = host_f32(c).astype(np.float64)
+    for r in range(m):
+        s = np.abs(a[r]).astype(np.float64).max() * np.abs(b).max()
+        tol = 1e-5 if r != 0 else 1e-3   # a subnormal row carries fewer than 24 bits itself
+        assert np.abs(got[r] - ref[r]).max() <= tol * s * np.sqrt(k), r

@@ -2,7 +2,7 @@
 
 It exists for callers that cannot allocate device memory when they issue the
 GEMM (plug-ins whose host framework owns the device allocator, host callbacks,
-fixed-budget real-time paths): its TF32 split planes live in a fixed 64 MiB device array inside
+fixed-budget real-time paths): its f16 split planes live in a fixed 64 MiB device array inside
 libipuc.so.  These tests call it through the C ABI and check it against the
 workspace entry point ipuc_gemm_f32 on two calls in a row (the second with new
 inputs, so leftover scratch contents would show), within the FP32 GEMM
