@@ -92,24 +92,60 @@ class TensorParallelBlock:
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
 
-    def forward(self, x):
+    def forward(self, x, chunks: int = 1):
         """x: [B*S, d] f16 on this GPU (the same on every rank); returns y
-        ([B*S, d], complete on every rank)."""
+        ([B*S, d], complete on every rank).
+
+        chunks > 1 (N > 1 only) pipelines the two row-split projections with
+        their all-reduces: the output projection and the MLP run in `chunks`
+        row blocks, each block's all-reduce is issued on a side stream as
+        soon as its GEMM is done, and the next block's GEMMs run meanwhile;
+        the MLP of a block waits only for that block's reduced rows."""
         torch = self.torch
-        s = torch.cuda.current_stream().cuda_stream
+        cur = torch.cuda.current_stream()
+        s = cur.cuda_stream
         T, d = self.B * self.S, self.d
         for w, out in ((self.wq, self.qf), (self.wk, self.kf), (self.wv, self.vf)):
             self._gemm(out, x, w, T, self.dl, d, 0, s)
         # Local heads read in place from [B, S, hl * dh] and written merged.
         call("ipuc_flash_attention_heads_f16", self.a.data_ptr(), F16, self.qf.data_ptr(), self.kf.data_ptr(),
              self.vf.data_ptr(), self.B, self.hl, self.S, self.S, self.dh, 0.0, s)
-        # h = x + sum over ranks of a_r Wo_r (rank 0's epilogue adds x).
-        self._gemm(self.h, self.a, self.wo, T, d, self.dl, 0, s, x if self.shard.adds_residual else None)
-        self._all_reduce(self.h)
-        # y = h + sum over ranks of GELU(h W1_r) W2_r.
-        self._gemm(self.u, self.h, self.w1, T, self.fl, d, GEMM_EPILOGUE_GELU, s)
-        self._gemm(self.y, self.u, self.w2, T, d, self.fl, 0, s, self.h if self.shard.adds_residual else None)
-        self._all_reduce(self.y)
+        res = self.shard.adds_residual
+        if chunks <= 1 or self.world == 1 or T % chunks:
+            # h = x + sum over ranks of a_r Wo_r (rank 0's epilogue adds x).
+            self._gemm(self.h, self.a, self.wo, T, d, self.dl, 0, s, x if res else None)
+            self._all_reduce(self.h)
+            # y = h + sum over ranks of GELU(h W1_r) W2_r.
+            self._gemm(self.u, self.h, self.w1, T, self.fl, d, GEMM_EPILOGUE_GELU, s)
+            self._gemm(self.y, self.u, self.w2, T, d, self.fl, 0, s, self.h if res else None)
+            self._all_reduce(self.y)
+            return self.y
+        import torch.distributed as dist
+        if getattr(self, "_comm", None) is None:
+            self._comm = torch.cuda.Stream()
+        comm = self._comm
+        rows = T // chunks
+        blocks = [slice(i * rows, (i + 1) * rows) for i in range(chunks)]
+
+        def reduce_async(t):
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            comm.wait_event(ev)
+            with torch.cuda.stream(comm):
+                return dist.all_reduce(t, group=self.group, async_op=True)
+
+        reduced_h = []
+        for r in blocks:
+            self._gemm(self.h[r], self.a[r], self.wo, rows, d, self.dl, 0, s, x[r] if res else None)
+            reduced_h.append(reduce_async(self.h[r]))
+        reduced_y = []
+        for r, work in zip(blocks, reduced_h):
+            work.wait()   # the compute stream waits for this block's reduced h
+            self._gemm(self.u[r], self.h[r], self.w1, rows, self.fl, d, GEMM_EPILOGUE_GELU, s)
+            self._gemm(self.y[r], self.u[r], self.w2, rows, d, self.fl, 0, s, self.h[r] if res else None)
+            reduced_y.append(reduce_async(self.y[r]))
+        for work in reduced_y:
+            work.wait()
         return self.y
 
     @property

@@ -29,11 +29,11 @@ def block_inputs():
     return inputs[x].reshape(B * S, d), weights, ref
 
 
-def run_rank(rank, world, x, weights):
+def run_rank(rank, world, x, weights, chunks=1):
     from ipuc.tp import TensorParallelBlock
     blk = TensorParallelBlock(B, S, d, H, ff, rank, world)
     blk.load({n: torch.from_numpy(a).half() for n, a in weights.items()})
-    y = blk.forward(torch.from_numpy(x).half().cuda())
+    y = blk.forward(torch.from_numpy(x).half().cuda(), chunks=chunks)
     torch.cuda.synchronize()
     return y.float().cpu().numpy()
 
@@ -53,7 +53,10 @@ def _nccl_worker(rank, world, port, q):
     try:
         x, weights, ref = block_inputs()
         got = run_rank(rank, world, x, weights)
-        q.put((rank,) + f16_close(got, ref))
+        # the row-chunked pipeline (all-reduce of each block overlapping the
+        # next block's GEMMs) computes the same sums
+        piped = run_rank(rank, world, x, weights, chunks=4)
+        q.put((rank,) + f16_close(got, ref) + f16_close(piped, ref))
     finally:
         dist.destroy_process_group()
 
@@ -74,5 +77,6 @@ def test_tp_block_two_ranks_nccl():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, ok, msg in res:
+    for rank, ok, msg, ok_piped, msg_piped in res:
         assert ok, f"rank {rank}: {msg}"
+        assert ok_piped, f"rank {rank}, chunks=4: {msg_piped}"
