@@ -444,25 +444,73 @@ def measure_components(ipuc, torch, stream, hbm_gbs):
         c32 = torch.empty((m, n_), device="cuda")
         ws = torch.empty(max(1, ipuc.gemm_f32_workspace_bytes(m, n_, k)), dtype=torch.uint8, device="cuda")
 
-        def run32():
-            ipuc.call("ipuc_gemm_f32", c32.data_ptr(), a32.data_ptr(), b32.data_ptr(), m, n_, k, k, n_, n_, 0,
-                      ws.data_ptr(), ws.numel(), s)
-        for _ in range(3):
-            run32()
-        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
-        a.record(stream)
-        for _ in range(10):
-            run32()
-        b.record(stream)
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / 10
-        out["gemm_f32_4096"] = {"ms": round(ms, 4), "tflops": round(2 * m * n_ * k / (ms * 1e-3) / 1e12, 1)}
+        def time32(flags):
+            def run32():
+                ipuc.call("ipuc_gemm_f32", c32.data_ptr(), a32.data_ptr(), b32.data_ptr(), m, n_, k, k, n_, n_,
+                          flags, ws.data_ptr(), ws.numel(), s)
+            for _ in range(3):
+                run32()
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record(stream)
+            for _ in range(10):
+                run32()
+            b.record(stream)
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / 10
+        ms = time32(0)                                   # default: scaled 3xF16 split
+        ms_tf32 = time32(ipuc.GEMM_F32_SPLIT_TF32)        # the classic 3xTF32 split, for comparison
+        flop32 = 2 * m * n_ * k
+        out["gemm_f32_4096"] = {"ms": round(ms, 4), "tflops": round(flop32 / (ms * 1e-3) / 1e12, 1),
+                                "split": "3xF16 scaled",
+                                "tflops_3xtf32": round(flop32 / (ms_tf32 * 1e-3) / 1e12, 1)}
     except ipuc.IpucError as e:
         out["gemm_f32_4096"] = {"unavailable": str(e)}
     del a32, b32, c32, ws
     torch.cuda.empty_cache()
+    out["gemm_f16_256"] = gemm_f16_small(ipuc, torch, stream)
     out["transformer_block"] = transformer_block(ipuc, torch, stream)
     return out
+
+
+def gemm_f16_small(ipuc, torch, stream):
+    """Config 1: the FP16 GEMM at 256^3 (3.36e7 FLOP), a latency case.  200
+    back-to-back launches on one stream (host launch rate included), and the same
+    200 launches captured in one CUDA graph (device time per GEMM)."""
+    m = n = k = 256
+    a = (torch.randn((m, k), device="cuda") * 0.1).half()
+    b = (torch.randn((k, n), device="cuda") * 0.1).half()
+    c = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    reps = 200
+
+    def run(s):
+        for _ in range(reps):
+            ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, 0, s)
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    run(stream.cuda_stream)
+    torch.cuda.synchronize()
+    us = timed(lambda: run(stream.cuda_stream))
+    res = {"us_per_gemm_stream": round(us, 2), "tflops_stream": round(2 * m * n * k / (us * 1e-6) / 1e12, 2)}
+    try:
+        side = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            run(side.cuda_stream)
+        graph.replay()
+        torch.cuda.synchronize()
+        us_g = timed(graph.replay)
+        res.update({"us_per_gemm_graph": round(us_g, 2),
+                    "tflops_graph": round(2 * m * n * k / (us_g * 1e-6) / 1e12, 2)})
+    except Exception as e:  # capture unsupported on this stack: keep the stream figure
+        res["graph"] = f"unavailable: {type(e).__name__}: {e}"[:200]
+    return res
 
 
 def transformer_block(ipuc, torch, stream):

@@ -33,9 +33,10 @@ namespace {
 
 using namespace sm100;
 
-// A k-block is one 128-byte swizzle row of each plane (64 f16 elements); an
-// MMA k-step (K16) is 32 bytes of it.
-constexpr int BM = 128, BN = 256, BK = 64, BK_BYTES = BK * 2, STAGES = 2;
+// A k-block is one 128-byte swizzle row of each plane: 64 f16 or 32 TF32
+// elements; an MMA k-step (K16 f16, K8 TF32) is 32 bytes of it either way, so
+// stage sizes and descriptor offsets are the same for both splits.
+constexpr int BM = 128, BN = 256, BK_BYTES = 128, STAGES = 2;
 constexpr int A_BYTES = BM * BK_BYTES;  // 16 KB per plane
 constexpr int B_BYTES = BN * BK_BYTES;  // 32 KB per plane
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // 96 KB
@@ -43,9 +44,102 @@ constexpr int TMEM_COLS = 2 * BN;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int GROUP_M = 16;
 constexpr int CHUNK_K = 256;     // K per TMEM accumulation chunk
-constexpr int KC = CHUNK_K / BK; // k-blocks per chunk
+template <bool kF16> struct Split {
+  static constexpr int BK = kF16 ? 64 : 32;            // elements per k-block
+  static constexpr int KC = CHUNK_K / BK;               // k-blocks per chunk
+  static constexpr uint32_t kFormat = kF16 ? 0u : 2u;   // instruction-descriptor A/B format
+};
 constexpr int EPI_THREADS = 256; // 8 epilogue warps
 constexpr int NUM_THREADS = 64 + EPI_THREADS;
+
+// Round to TF32 (10 explicit mantissa bits), nearest, ties away from zero.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// 3xTF32 (IPUC_GEMM_F32_SPLIT_TF32): hi/lo planes of a row-major [rows x cols]
+// matrix with leading dimension ld into dense [rows x cols] fp32 planes, with
+// hi = tf32(x) and lo = tf32(x - hi); no scaling (TF32 has fp32's exponent).
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                         int64_t ld, float *__restrict__ hi, float *__restrict__ lo) {
+  const int64_t total4 = rows * cols / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
+    const int64_t e = i * 4, r = e / cols, c = e % cols;
+    const float4 x = *reinterpret_cast<const float4 *>(src + r * ld + c);
+    float4 h, l;
+    h.x = to_tf32(x.x); l.x = to_tf32(x.x - h.x);
+    h.y = to_tf32(x.y); l.y = to_tf32(x.y - h.y);
+    h.z = to_tf32(x.z); l.z = to_tf32(x.z - h.z);
+    h.w = to_tf32(x.w); l.w = to_tf32(x.w - h.w);
+    reinterpret_cast<float4 *>(hi)[i] = h;
+    reinterpret_cast<float4 *>(lo)[i] = l;
+  }
+}
+
+// hi/lo planes of B^T: B is row-major [rows x cols] (ld); the planes are dense
+// [cols x rows], so the MMA reads B K-major.  64x64 tiles through shared memory,
+// 16-byte loads and stores (each thread moves 16 elements each way) so that
+// enough bytes are in flight per SM to run near HBM bandwidth; the padded tile
+// row (65 floats) keeps the column reads conflict-free.  Vector accesses need
+// rows, cols and ld to be multiples of 4 (the gemm_f32 entry requires that);
+// ragged 64x64 tiles fall back to scalar accesses.
+__global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float *__restrict__ src, int64_t rows,
+                                                                   int64_t cols, int64_t ld, float *__restrict__ hi,
+                                                                   float *__restrict__ lo) {
+  __shared__ float tile[64][65];
+  const int64_t tr = (rows + 63) / 64, tc = (cols + 63) / 64;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 16 threads, 4 consecutive elements each
+  for (int64_t t = blockIdx.x; t < tr * tc; t += gridDim.x) {
+    const int64_t r0 = (t / tc) * 64, c0 = (t % tc) * 64;
+    const bool full = r0 + 64 <= rows && c0 + 64 <= cols;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = ty + 16 * i, cc = tx * 4;
+      const int64_t r = r0 + rr, c = c0 + cc;
+      float4 v;
+      if (full) {
+        v = *reinterpret_cast<const float4 *>(src + r * ld + c);
+      } else {
+        v.x = (r < rows && c < cols) ? src[r * ld + c] : 0.0f;
+        v.y = (r < rows && c + 1 < cols) ? src[r * ld + c + 1] : 0.0f;
+        v.z = (r < rows && c + 2 < cols) ? src[r * ld + c + 2] : 0.0f;
+        v.w = (r < rows && c + 3 < cols) ? src[r * ld + c + 3] : 0.0f;
+      }
+      tile[rr][cc] = v.x;
+      tile[rr][cc + 1] = v.y;
+      tile[rr][cc + 2] = v.z;
+      tile[rr][cc + 3] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int oc = ty + 16 * i, orr = tx * 4;  // output row = source column c0 + oc
+      const int64_t c = c0 + oc, r = r0 + orr;
+      float x[4], h[4], l[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[e] = tile[orr + e][oc];
+        h[e] = to_tf32(x[e]);
+        l[e] = to_tf32(x[e] - h[e]);
+      }
+      if (full) {
+        *reinterpret_cast<float4 *>(hi + c * rows + r) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4 *>(lo + c * rows + r) = make_float4(l[0], l[1], l[2], l[3]);
+      } else if (c < cols) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (r + e < rows) {
+            hi[c * rows + r + e] = h[e];
+            lo[c * rows + r + e] = l[e];
+          }
+      }
+    }
+  }
+}
 
 // ---- 3xF16 split with power-of-two row/column scaling ----
 // f16 has TF32's 10 explicit mantissa bits but only a 5-bit exponent, so each
@@ -268,8 +362,20 @@ __device__ __forceinline__ void tile_coords(const Gemm32Params &p, int64_t t, in
   nt = (int)(w / gs);
 }
 
+template <bool kF16>
+__device__ __forceinline__ void mma_split(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (kF16) mma_f16_ss(d, a, b, idesc, acc);
+  else mma_tf32_ss(d, a, b, idesc, acc);
+}
+template <bool kF16>
+__device__ __forceinline__ void mma_split_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  if constexpr (kF16) mma_f16_ss_pair(d, a, b, idesc, acc);
+  else mma_tf32_ss_pair(d, a, b, idesc, acc);
+}
+
+template <bool kF16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+    gemm_split3_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                        const Gemm32Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -302,6 +408,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  constexpr int BK = Split<kF16>::BK, KC = Split<kF16>::KC;
   const int chunks = (p.k_blocks + KC - 1) / KC;
 
   if (warp == 0) {
@@ -334,7 +441,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BM, BN, /*f16*/ 0, false, false);
+      constexpr uint32_t idesc = make_idesc(BM, BN, Split<kF16>::kFormat, false, false);
       uint32_t it = 0, g = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
@@ -358,15 +465,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t ah = smem_u32(smem + s * STAGE_BYTES), al = ah + A_BYTES;
             const uint32_t bh = ah + 2 * A_BYTES, bl = bh + B_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK_BYTES / 32; ++k) {  // K16 steps of 32 bytes
+            for (int k = 0; k < BK_BYTES / 32; ++k) {  // 32-byte k-steps
               const uint64_t dah = make_smem_desc(ah + k * 32, 16, 1024, kSwizzle128B);
               const uint64_t dal = make_smem_desc(al + k * 32, 16, 1024, kSwizzle128B);
               const uint64_t dbh = make_smem_desc(bh + k * 32, 16, 1024, kSwizzle128B);
               const uint64_t dbl = make_smem_desc(bl + k * 32, 16, 1024, kSwizzle128B);
               // Small terms first, then the dominant hi.hi product.
-              mma_f16_ss(d_tmem, dal, dbh, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
-              mma_f16_ss(d_tmem, dah, dbl, idesc, 1u);
-              mma_f16_ss(d_tmem, dah, dbh, idesc, 1u);
+              mma_split<kF16>(d_tmem, dal, dbh, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
+              mma_split<kF16>(d_tmem, dah, dbl, idesc, 1u);
+              mma_split<kF16>(d_tmem, dah, dbh, idesc, 1u);
             }
             mma_commit(&empty[s]);
           }
@@ -417,14 +524,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t row = (int64_t)mt * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
-        const int er = p.ea[row];
+        const int er = kF16 ? p.ea[row] : 0;
         float *cp = p.c + row * p.ldc + col_base;
         if (vec_ok && col_base + BN / 2 <= p.n) {
           float4 *c4 = reinterpret_cast<float4 *>(cp);
 #pragma unroll
           for (int j = 0; j < BN / 8; ++j) {
             float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-            {
+            if constexpr (kF16) {
               const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col_base) + j);
               v.x = unscale(v.x, er, ec.x);
               v.y = unscale(v.y, er, ec.y);
@@ -442,7 +549,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int j = 0; j < BN / 2; ++j) {
             if (col_base + j < p.n) {
               float x = acc[j];
-              x = unscale(x, er, p.eb[col_base + j]);
+              if constexpr (kF16) x = unscale(x, er, p.eb[col_base + j]);
               if (accumulate) x += cp[j];
               cp[j] = x;
             }
@@ -473,8 +580,9 @@ constexpr int P_STAGES = 3;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr int PAIR_BM = 2 * BM;
 
+template <bool kF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-    gemm_f16x3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+    gemm_split3_pair_kernel(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                             const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl,
                             const Gemm32Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -510,6 +618,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  constexpr int BK = Split<kF16>::BK, KC = Split<kF16>::KC;
   const int chunks = (p.k_blocks + KC - 1) / KC;
 
   if (warp == 0) {
@@ -542,7 +651,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*f16*/ 0, false, false);
+      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, Split<kF16>::kFormat, false, false);
       // Descriptors built once; stages and k-steps add offsets in 16-byte units.
       const uint64_t d0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       uint32_t it = 0, g = 0;
@@ -570,12 +679,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const uint64_t dbh = dah + (uint64_t)((2 * A_BYTES) >> 4);
             const uint64_t dbl = dah + (uint64_t)((3 * A_BYTES) >> 4);
 #pragma unroll
-            for (int k = 0; k < BK_BYTES / 32; ++k) {  // K16 steps of 32 bytes
+            for (int k = 0; k < BK_BYTES / 32; ++k) {  // 32-byte k-steps
               const uint64_t o = (uint64_t)((k * 32) >> 4);
               // Small terms first, then the dominant hi.hi product.
-              mma_f16_ss_pair(d_tmem, dal + o, dbh + o, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
-              mma_f16_ss_pair(d_tmem, dah + o, dbl + o, idesc, 1u);
-              mma_f16_ss_pair(d_tmem, dah + o, dbh + o, idesc, 1u);
+              mma_split_pair<kF16>(d_tmem, dal + o, dbh + o, idesc, (kb != c * KC || k != 0) ? 1u : 0u);
+              mma_split_pair<kF16>(d_tmem, dah + o, dbl + o, idesc, 1u);
+              mma_split_pair<kF16>(d_tmem, dah + o, dbh + o, idesc, 1u);
             }
             mma_commit_pair(&empty[s], 0x3);
           }
@@ -625,14 +734,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
-        const int er = p.ea[row];
+        const int er = kF16 ? p.ea[row] : 0;
         float *cp = p.c + row * p.ldc + col_base;
         if (vec_ok && col_base + BN / 2 <= p.n) {
           float4 *c4 = reinterpret_cast<float4 *>(cp);
 #pragma unroll
           for (int j = 0; j < BN / 8; ++j) {
             float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-            {
+            if constexpr (kF16) {
               const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col_base) + j);
               v.x = unscale(v.x, er, ec.x);
               v.y = unscale(v.y, er, ec.y);
@@ -650,7 +759,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           for (int j = 0; j < BN / 2; ++j) {
             if (col_base + j < p.n) {
               float x = acc[j];
-              x = unscale(x, er, p.eb[col_base + j]);
+              if constexpr (kF16) x = unscale(x, er, p.eb[col_base + j]);
               if (accumulate) x += cp[j];
               cp[j] = x;
             }
@@ -674,15 +783,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 inline uint64_t round256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
-// Workspace: A_hi, A_lo [m x kp] and B_hi, B_lo [n x kp] f16 (kp = k rounded
-// up to 8, so that plane rows are 16-byte multiples for TMA), then the split
-// exponents of A's rows [m] and B's columns [n] (int32) and B's column maxima
-// [n] (u32 float bits, row-major B only), each 256-byte aligned.
+// Workspace, 3xF16: A_hi, A_lo [m x kp] and B_hi, B_lo [n x kp] f16 (kp = k
+// rounded up to 8, so that plane rows are 16-byte multiples for TMA), then the
+// split exponents of A's rows [m] and B's columns [n] (int32) and B's column
+// maxima [n] (u32 float bits, row-major B only), each 256-byte aligned.
+// 3xTF32: A_hi, A_lo [m x k] and B_hi, B_lo [n x k] fp32.  The workspace size
+// is the larger of the two.
 int64_t f16_pitch(int64_t k) { return (k + 7) & ~int64_t(7); }
+uint64_t tf32_workspace(int64_t m, int64_t n, int64_t k) {
+  return 2 * round256((uint64_t)m * k * 4) + 2 * round256((uint64_t)k * n * 4);
+}
 
+template <bool kF16>
 ipuc_status launch_main(const CUtensorMap &tah, const CUtensorMap &tal, void *bh, void *bl, int64_t m, int64_t n,
                         int64_t k, int64_t ldp, Gemm32Params &p, cudaStream_t stream) {
-  const auto dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  constexpr int BK = Split<kF16>::BK;
+  const auto dt = kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const size_t eb = kF16 ? 2 : 4;
   ipuc_status st;
   p.tiles_n = (int32_t)((n + BN - 1) / BN);
   p.k_blocks = (int32_t)((k + BK - 1) / BK);
@@ -693,41 +810,50 @@ ipuc_status launch_main(const CUtensorMap &tah, const CUtensorMap &tal, void *bh
     // single-CTA kernel spreads the work over more SMs): A boxes of 128 rows
     // per CTA, B boxes of 128 rows (half of BN).
     CUtensorMap pbh, pbl;
-    if ((st = make_map_3d(&pbh, dt, 2, bh, k, n, 1, ldp, 0, BK, BN / 2)) != IPUC_OK) return st;
-    if ((st = make_map_3d(&pbl, dt, 2, bl, k, n, 1, ldp, 0, BK, BN / 2)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&pbh, dt, eb, bh, k, n, 1, ldp, 0, BK, BN / 2)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&pbl, dt, eb, bl, k, n, 1, ldp, 0, BK, BN / 2)) != IPUC_OK) return st;
     p.tiles_m = (int32_t)((m + PAIR_BM - 1) / PAIR_BM);
     p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
     const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
-    IPUC_CUDA(cudaFuncSetAttribute(gemm_f16x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-    gemm_f16x3_pair_kernel<<<(unsigned)(2 * pairs), NUM_THREADS, P_SMEM_BYTES, stream>>>(tah, tal, pbh, pbl, p);
-    return check_launch("gemm_f16x3_pair_kernel");
+    IPUC_CUDA(cudaFuncSetAttribute(gemm_split3_pair_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   P_SMEM_BYTES));
+    gemm_split3_pair_kernel<kF16><<<(unsigned)(2 * pairs), NUM_THREADS, P_SMEM_BYTES, stream>>>(tah, tal, pbh, pbl, p);
+    return check_launch("gemm_split3_pair_kernel");
   }
   CUtensorMap tbh, tbl;
-  if ((st = make_map_3d(&tbh, dt, 2, bh, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
-  if ((st = make_map_3d(&tbl, dt, 2, bl, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
+  if ((st = make_map_3d(&tbh, dt, eb, bh, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
+  if ((st = make_map_3d(&tbl, dt, eb, bl, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
   p.tiles_m = (int32_t)((m + BM - 1) / BM);
   p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
   const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
-  IPUC_CUDA(cudaFuncSetAttribute(gemm_f16x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  gemm_f16x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tah, tal, tbh, tbl, p);
-  return check_launch("gemm_f16x3_kernel");
+  IPUC_CUDA(cudaFuncSetAttribute(gemm_split3_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  gemm_split3_kernel<kF16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tah, tal, tbh, tbl, p);
+  return check_launch("gemm_split3_kernel");
 }
 
 }  // namespace
 
-uint64_t gemm_f32_workspace(int64_t m, int64_t n, int64_t k) {
+// Bytes of workspace the split named by `flags` uses.
+uint64_t gemm_f32_workspace_for(int64_t m, int64_t n, int64_t k, uint32_t flags) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
+  if (flags & IPUC_GEMM_F32_SPLIT_TF32) return tf32_workspace(m, n, k);
   const uint64_t kp = (uint64_t)f16_pitch(k);
   return 2 * round256((uint64_t)m * kp * 2) + 2 * round256((uint64_t)n * kp * 2) + round256((uint64_t)m * 4) +
          2 * round256((uint64_t)n * 4);
+}
+
+// ipuc_gemm_f32_workspace_bytes: enough for either split.
+uint64_t gemm_f32_workspace(int64_t m, int64_t n, int64_t k) {
+  const uint64_t a = gemm_f32_workspace_for(m, n, k, 0), b = gemm_f32_workspace_for(m, n, k, IPUC_GEMM_F32_SPLIT_TF32);
+  return a > b ? a : b;
 }
 
 ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m, int64_t n, int64_t k, int64_t lda,
                             int64_t ldb, int64_t ldc, uint32_t flags, void *workspace, uint64_t workspace_bytes,
                             cudaStream_t stream) {
   IPUC_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "gemm_f32: negative extent");
-  IPUC_CHECK_ARG((flags & ~(uint32_t)(IPUC_GEMM_ACCUMULATE | IPUC_GEMM_B_TRANSPOSED)) == 0,
-                 "gemm_f32: only IPUC_GEMM_ACCUMULATE and IPUC_GEMM_B_TRANSPOSED apply");
+  IPUC_CHECK_ARG((flags & ~(uint32_t)(IPUC_GEMM_ACCUMULATE | IPUC_GEMM_B_TRANSPOSED | IPUC_GEMM_F32_SPLIT_TF32)) == 0,
+                 "gemm_f32: only IPUC_GEMM_ACCUMULATE, IPUC_GEMM_B_TRANSPOSED and IPUC_GEMM_F32_SPLIT_TF32 apply");
   if (m == 0 || n == 0) return IPUC_OK;
   IPUC_CHECK_ARG(k > 0, "gemm_f32: k must be positive");
   IPUC_CHECK_ARG(a && b && c, "gemm_f32: null pointer");
@@ -737,7 +863,7 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
   IPUC_CHECK_ALIGN(lda % 4 == 0 && ldb % 4 == 0 && k % 4 == 0 && n % 4 == 0,
                    "gemm_f32: lda, ldb, k and n must be multiples of 4 elements");
   IPUC_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31), "gemm_f32: extent too large");
-  const uint64_t need = gemm_f32_workspace(m, n, k);
+  const uint64_t need = gemm_f32_workspace_for(m, n, k, flags);
   IPUC_CHECK_ARG(workspace != nullptr && workspace_bytes >= need,
                  "gemm_f32: workspace smaller than ipuc_gemm_f32_workspace_bytes()");
   IPUC_CHECK_ALIGN(aligned(workspace, 256), "gemm_f32: workspace must be 256-byte aligned");
@@ -754,7 +880,7 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
   ipuc_status st;
   CUtensorMap tah, tal;
 
-  {
+  if (!(flags & IPUC_GEMM_F32_SPLIT_TF32)) {
     const int64_t kp = f16_pitch(k);
     __half *ah = reinterpret_cast<__half *>(ws);
     __half *al = reinterpret_cast<__half *>(ws + round256((uint64_t)m * kp * 2));
@@ -778,12 +904,34 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
     }
     if ((st = check_launch("gemm_f32 split (3xF16)")) != IPUC_OK) return st;
     const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if ((st = make_map_3d(&tah, f16, 2, ah, k, m, 1, kp, 0, BK, BM)) != IPUC_OK) return st;
-    if ((st = make_map_3d(&tal, f16, 2, al, k, m, 1, kp, 0, BK, BM)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&tah, f16, 2, ah, k, m, 1, kp, 0, Split<true>::BK, BM)) != IPUC_OK) return st;
+    if ((st = make_map_3d(&tal, f16, 2, al, k, m, 1, kp, 0, Split<true>::BK, BM)) != IPUC_OK) return st;
     p.ea = ea;
     p.eb = eb;
-    return launch_main(tah, tal, bh, bl, m, n, k, kp, p, stream);
+    return launch_main<true>(tah, tal, bh, bl, m, n, k, kp, p, stream);
   }
+
+  // 3xTF32: unscaled TF32 hi/lo planes, fp32 storage.
+  float *ah = reinterpret_cast<float *>(ws);
+  float *al = reinterpret_cast<float *>(ws + round256((uint64_t)m * k * 4));
+  float *bh = reinterpret_cast<float *>(ws + 2 * round256((uint64_t)m * k * 4));
+  float *bl = reinterpret_cast<float *>(ws + 2 * round256((uint64_t)m * k * 4) + round256((uint64_t)k * n * 4));
+  auto grid_of = [&](int64_t threads) {
+    const int64_t g = (threads + 255) / 256;
+    return (unsigned)(g < cap ? (g < 1 ? 1 : g) : cap);
+  };
+  split_tf32_kernel<<<grid_of(m * k / 4), 256, 0, stream>>>(a, m, k, lda, ah, al);
+  if (bt) {
+    split_tf32_kernel<<<grid_of(n * k / 4), 256, 0, stream>>>(b, n, k, ldb, bh, bl);
+  } else {
+    const int64_t tiles = ((k + 63) / 64) * ((n + 63) / 64);
+    split_tf32_transpose_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(b, k, n, ldb, bh, bl);
+  }
+  if ((st = check_launch("gemm_f32 split (3xTF32)")) != IPUC_OK) return st;
+  const auto f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  if ((st = make_map_3d(&tah, f32, 4, ah, k, m, 1, k, 0, Split<false>::BK, BM)) != IPUC_OK) return st;
+  if ((st = make_map_3d(&tal, f32, 4, al, k, m, 1, k, 0, Split<false>::BK, BM)) != IPUC_OK) return st;
+  return launch_main<false>(tah, tal, bh, bl, m, n, k, k, p, stream);
 }
 
 }  // namespace ipuc
@@ -849,12 +997,13 @@ ipuc_status scratch_address(void **out) {
 extern "C" ipuc_status ipuc_gemm_f32_noalloc(float *c, const float *a, const float *b, int64_t m, int64_t n,
                                              int64_t k, int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags,
                                              ipuc_stream stream) {
-  const uint64_t need = ipuc::gemm_f32_workspace(m, n, k);
+  const uint64_t need = ipuc::gemm_f32_workspace_for(m, n, k, flags);
   if (need > ipuc::kNoAllocScratchBytes) {
     char buf[320];
     snprintf(buf, sizeof(buf),
              "gemm_f32_noalloc: m=%lld n=%lld k=%lld needs %llu scratch bytes, above the fixed %llu-byte array "
-             "(about 4*(m + n)*k <= 64 MiB); use ipuc_gemm_f32 with a workspace",
+             "(about 4*(m + n)*k, or 8*(m + n)*k with IPUC_GEMM_F32_SPLIT_TF32, <= 64 MiB); use ipuc_gemm_f32 "
+             "with a workspace",
              (long long)m, (long long)n, (long long)k, (unsigned long long)need,
              (unsigned long long)ipuc::kNoAllocScratchBytes);
     return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, buf);

@@ -27,6 +27,7 @@ F16, F32 = 0, 1
  BLOCK_MAJOR, BLOCK_MAJOR_TRANSPOSED) = range(8)
 # gemm flags
 GEMM_ACCUMULATE, GEMM_B_TRANSPOSED, GEMM_OUT_F32, GEMM_EPILOGUE_GELU = 1, 2, 4, 8
+GEMM_F32_SPLIT_TF32 = 16  # ipuc_gemm_f32: the unscaled 3xTF32 split instead of the scaled f16 one
 
 # Every exported entry point with its argument types (kept in sync with
 # include/ipuc.h; tests check the library exports each one).

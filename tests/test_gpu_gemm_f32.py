@@ -1,4 +1,5 @@
-"""Parity of the three-pass f16-split FP32 GEMM (gemm_f32_64_amp replacement)
+"""Parity of the FP32 GEMM (gemm_f32_64_amp replacement): the default scaled
+three-pass f16 split and the three-pass TF32 split (IPUC_GEMM_F32_SPLIT_TF32)
 against the oracle's f32 SGEMM (diagnostic.rs:581-654).  BASELINE tolerance:
 rel-L2 <= 1e-5."""
 import numpy as np
@@ -30,11 +31,15 @@ def run(m, n, k, flags=0, c0=None, seed=0):
     return host_f32(c), ref, a, b
 
 
+SPLITS = [0, ipuc.GEMM_F32_SPLIT_TF32]   # default scaled 3xF16, and 3xTF32
+
+
 @pytest.mark.parametrize("m,n,k", [(256, 256, 256), (128, 512, 64), (300, 260, 100), (1, 4, 4), (1024, 1024, 1024),
                                    (4096, 4096, 4096)])
 @pytest.mark.parametrize("bt", [False, True])
-def test_gemm_f32_rel_l2(m, n, k, bt):
-    got, ref, a, b = run(m, n, k, ipuc.GEMM_B_TRANSPOSED if bt else 0, seed=m + k)
+@pytest.mark.parametrize("split", SPLITS)
+def test_gemm_f32_rel_l2(m, n, k, bt, split):
+    got, ref, a, b = run(m, n, k, (ipuc.GEMM_B_TRANSPOSED if bt else 0) | split, seed=m + k)
     assert rel_l2(got, ref) <= 1e-5
     if m * n * k <= 1 << 27:
         # also against the f32 BLAS evaluator itself
@@ -42,18 +47,20 @@ def test_gemm_f32_rel_l2(m, n, k, bt):
         assert rel_l2(got, blas.astype(np.float64)) <= 1e-5
 
 
-def test_gemm_f32_accumulate():
+@pytest.mark.parametrize("split", SPLITS)
+def test_gemm_f32_accumulate(split):
     c0 = seeded_uniform(9, (200, 136))
-    got, ref, _, _ = run(200, 136, 520, ipuc.GEMM_ACCUMULATE, c0=c0, seed=4)
+    got, ref, _, _ = run(200, 136, 520, ipuc.GEMM_ACCUMULATE | split, c0=c0, seed=4)
     assert rel_l2(got, ref) <= 1e-5
 
 
 @pytest.mark.parametrize("bt", [False, True])
-def test_gemm_f32_pair_path_ragged(bt):
+@pytest.mark.parametrize("split", SPLITS)
+def test_gemm_f32_pair_path_ragged(bt, split):
     """At least a wave of 256x256 tiles takes the CTA-pair kernel: ragged rows
     (2200 = 8.6 pair tiles), a column tail (4104 = 16 * 256 + 8) and a K tail
     (200 = 6.25 blocks of 32)."""
-    got, ref, _, _ = run(2200, 4104, 200, ipuc.GEMM_B_TRANSPOSED if bt else 0, seed=31)
+    got, ref, _, _ = run(2200, 4104, 200, (ipuc.GEMM_B_TRANSPOSED if bt else 0) | split, seed=31)
     assert rel_l2(got, ref) <= 1e-5
 
 
