@@ -123,7 +123,8 @@ ipuc_status ipug_profile_encode(uint64_t clock_hz, const ipug_profile_tile *tile
  * normally the GPU's rank): clockHz 1e9, so a cycle is one nanosecond from the
  * first event; one Compute step per lowered step, operation "operation.<id>"
  * of its first graph operation, kernel = the step's kernel, metadata
- * "operations" (all fused op ids), "flop"/"tflops" or "bytes"/"gbs", "device". */
+ * "operations" (all fused op ids), "flop"/"tflops" or "bytes"/"gbs", "device".
+ * Cycle counts are u32 in the schema: they saturate at 2^32 - 1 ns (4.29 s). */
 ipuc_status ipug_session_profile_capnp(ipug_session *s, ipuc_stream stream, uint32_t physical_tile, void *buf,
                                        uint64_t size, uint64_t *needed);
 

@@ -39,8 +39,13 @@ ipuc_status fail(ipuc_status st, const std::string &msg);
 
 namespace ipug_capnp {
 
+// List pointers carry element and word counts in 29 bits; larger lists or
+// texts make the builder fail instead of wrapping.
+constexpr uint64_t kMaxListCount = (1ull << 29) - 1;
+
 class Builder {
  public:
+  bool overflow = false;
   // Allocate n zeroed words; returns the index of the first.
   uint32_t alloc(uint32_t n) {
     const uint32_t at = static_cast<uint32_t>(w_.size());
@@ -66,6 +71,10 @@ class Builder {
   // Composite list of n structs at pointer `ptr`; returns the first element's word.
   uint32_t new_struct_list(uint32_t ptr, uint32_t n, uint16_t data_words, uint16_t ptr_words) {
     const uint32_t per = data_words + ptr_words;
+    if ((uint64_t)n * per > kMaxListCount || w_.size() + 1 + (uint64_t)n * per > kMaxListCount) {
+      overflow = true;
+      return alloc(0);
+    }
     const uint32_t tag = alloc(1 + n * per);
     w_[tag] = (static_cast<uint64_t>(n) << 2) | (uint64_t(data_words) << 32) | (uint64_t(ptr_words) << 48);
     list_ptr(ptr, tag, 7, n * per);
@@ -74,6 +83,10 @@ class Builder {
   // Text (NUL-terminated byte list) at pointer `ptr`.
   void text(uint32_t ptr, const char *s) {
     const size_t len = s ? std::strlen(s) : 0;
+    if (len + 1 > kMaxListCount || w_.size() + (len + 8) / 8 > kMaxListCount) {
+      overflow = true;
+      return;
+    }
     const uint32_t at = alloc(static_cast<uint32_t>((len + 1 + 7) / 8));
     if (len) std::memcpy(bytes(at), s, len);
     list_ptr(ptr, at, 2, static_cast<uint32_t>(len + 1));
@@ -99,6 +112,10 @@ class Builder {
 
 constexpr uint32_t kSchemaVersion = 5;  // crates/ipu-package/src/lib.rs:201,262
 
+ipuc_status too_large() {
+  return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "profile_encode: report larger than a Cap'n Proto segment");
+}
+
 ipuc_status encode(uint64_t clock_hz, const ipug_profile_tile *tiles, uint64_t tile_count, std::string &out) {
   if (tile_count && !tiles) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "profile_encode: null tiles");
   if (tile_count > 0x1FFFFFFFu) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "profile_encode: too many tiles");
@@ -108,6 +125,7 @@ ipuc_status encode(uint64_t clock_hz, const ipug_profile_tile *tiles, uint64_t t
   b.put32(root, 0, kSchemaVersion);
   b.put64(root, 8, clock_hz);
   const uint32_t tile0 = b.new_struct_list(root + 2, static_cast<uint32_t>(tile_count), 1, 1);
+  if (b.overflow) return too_large();
   for (uint64_t t = 0; t < tile_count; ++t) {
     const ipug_profile_tile &tile = tiles[t];
     if (tile.sample_count && !tile.samples)
@@ -117,6 +135,7 @@ ipuc_status encode(uint64_t clock_hz, const ipug_profile_tile *tiles, uint64_t t
     const uint32_t tw = tile0 + static_cast<uint32_t>(t) * 2;
     b.put32(tw, 0, tile.physical_tile);
     const uint32_t s0 = b.new_struct_list(tw + 1, static_cast<uint32_t>(tile.sample_count), 1, 1);
+    if (b.overflow) return too_large();
     for (uint64_t i = 0; i < tile.sample_count; ++i) {
       const ipug_profile_sample &sm = tile.samples[i];
       if (sm.kind > IPUG_STEP_IDLE) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "profile_encode: step kind out of range");
@@ -136,11 +155,13 @@ ipuc_status encode(uint64_t clock_hz, const ipug_profile_tile *tiles, uint64_t t
       b.text(st + 3, sm.operation);
       b.text(st + 4, sm.kernel);
       const uint32_t m0 = b.new_struct_list(st + 5, sm.metadata_count, 0, 2);
+      if (b.overflow) return too_large();
       for (uint32_t j = 0; j < sm.metadata_count; ++j) {
         b.text(m0 + 2 * j, sm.metadata[2 * j]);
         b.text(m0 + 2 * j + 1, sm.metadata[2 * j + 1]);
       }
       const uint32_t a0 = b.new_struct_list(st + 6, sm.activity_count, 2, 0);
+      if (b.overflow) return too_large();
       for (uint32_t j = 0; j < sm.activity_count; ++j) {
         const ipug_exchange_activity &a = sm.activities[j];
         if (a.kind > 2) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "profile_encode: activity kind out of range");
@@ -150,6 +171,7 @@ ipuc_status encode(uint64_t clock_hz, const ipug_profile_tile *tiles, uint64_t t
       }
     }
   }
+  if (b.overflow) return too_large();
   out = b.frame();
   return IPUC_OK;
 }
