@@ -436,6 +436,33 @@ def measure_components(ipuc, torch, stream, hbm_gbs):
         gbs = 2 * n * 2 / (ms * 1e-3) / 1e9
         out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3)}
     del src, dst
+    torch.cuda.empty_cache()
+    # Config 3's unfused stages: split-K reduce of 4 fp32 partials -> f16
+    # (4 x 512 MiB read + 256 MiB written) and standalone GELU (256 MiB each way).
+    cnt = MLP_M * MLP_N
+    parts = torch.randn((4, cnt), device="cuda", dtype=torch.float32)
+    y16 = torch.empty(cnt, device="cuda", dtype=torch.float16)
+    g16 = torch.empty(cnt, device="cuda", dtype=torch.float16)
+    stages = [
+        ("reduce_add_splitk4", 4 * cnt * 4 + cnt * 2,
+         ("ipuc_reduce_sum", y16.data_ptr(), parts[0].data_ptr(), parts[1].data_ptr(), 3, cnt, ipuc.F32, s)),
+        ("gelu_f16", 2 * cnt * 2, ("ipuc_gelu_f16", g16.data_ptr(), y16.data_ptr(), cnt, s)),
+    ]
+    for name, nbytes, args in stages:
+        for _ in range(3):
+            ipuc.call(*args)
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(stream)
+        for _ in range(10):
+            ipuc.call(*args)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 10
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3),
+                     "bytes": nbytes}
+    del parts, y16, g16
+    torch.cuda.empty_cache()
     # FP32 GEMM 4096^3 (3xF16 split)
     try:
         m = n_ = k = 4096

@@ -18,16 +18,30 @@ unsigned grid_for(int64_t chunks, int threads) {
 __global__ void __launch_bounds__(256) gelu_f16_kernel(uint4 *__restrict__ out, const uint4 *__restrict__ in,
                                                        int64_t chunks, const uint16_t *__restrict__ tail_in,
                                                        uint16_t *__restrict__ tail_out, int tail) {
+  // Four 16-byte chunks per thread and iteration (stride apart), all loaded
+  // before any is computed, so that enough bytes are in flight per SM for the
+  // kernel to stay HBM-bound.
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += stride) {
-    uint4 v = in[i];
-    uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+  auto apply = [](uint4 &v) {
+    __half2 *w = reinterpret_cast<__half2 *>(&v);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float a = h2f((uint16_t)(w[j] & 0xffffu)), b = h2f((uint16_t)(w[j] >> 16));
-      w[j] = pack_h2(gelu_f32(a), gelu_f32(b));
+      const float2 f = __half22float2(w[j]);
+      w[j] = __floats2half2_rn(gelu_f32(f.x), gelu_f32(f.y));
     }
-    out[i] = v;
+  };
+  constexpr int U = 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += U * stride) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i + u * stride < chunks) v[u] = in[i + u * stride];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i + u * stride < chunks) {
+        apply(v[u]);
+        out[i + u * stride] = v[u];
+      }
   }
   if (blockIdx.x == 0 && (int)threadIdx.x < tail) tail_out[threadIdx.x] = f2h(gelu_f32(h2f(tail_in[threadIdx.x])));
 }
