@@ -462,6 +462,29 @@ def measure_components(ipuc, torch, stream, hbm_gbs):
         out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3),
                      "bytes": nbytes}
     del parts, y16, g16
+    # Config 5's residual Add (8192 x 4096 f16: two reads, one write) and a
+    # Cast of the same activation f16 -> f32 (2 bytes read, 4 written).
+    na = 8192 * 4096
+    l16, r16 = (torch.randn(na, device="cuda").half() for _ in range(2))
+    o16 = torch.empty(na, device="cuda", dtype=torch.float16)
+    o32 = torch.empty(na, device="cuda", dtype=torch.float32)
+    for name, nbytes, args in [
+        ("add_f16", 3 * na * 2, ("ipuc_add_f16", o16.data_ptr(), l16.data_ptr(), r16.data_ptr(), na, 0, 0, s)),
+        ("cast_f16_to_f32", na * 6, ("ipuc_cast", o32.data_ptr(), ipuc.F32, l16.data_ptr(), ipuc.F16, na, s)),
+    ]:
+        for _ in range(3):
+            ipuc.call(*args)
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(stream)
+        for _ in range(10):
+            ipuc.call(*args)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 10
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / hbm_gbs, 3),
+                     "bytes": nbytes}
+    del l16, r16, o16, o32
     torch.cuda.empty_cache()
     # FP32 GEMM 4096^3 (3xF16 split)
     try:

@@ -109,6 +109,55 @@ __global__ void __launch_bounds__(256) add_f16_kernel(uint16_t *__restrict__ out
   }
 }
 
+// f16 <-> f32 in 8-element chunks: one 16-byte f16 access and two 16-byte f32
+// accesses per chunk (16-byte aligned pointers; the tail goes through
+// cast_kernel).
+template <bool kToF32>
+__global__ void __launch_bounds__(256) cast_vec_kernel(void *__restrict__ out, const void *__restrict__ in,
+                                                       int64_t chunks) {
+  // Four chunks per thread and iteration, all loaded before any is stored.
+  constexpr int U = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += U * stride) {
+    if constexpr (kToF32) {
+      uint4 h[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * stride < chunks) h[u] = reinterpret_cast<const uint4 *>(in)[i + u * stride];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (i + u * stride >= chunks) break;
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&h[u]);
+        const float2 a = __half22float2(h2[0]), b = __half22float2(h2[1]), c = __half22float2(h2[2]),
+                     d = __half22float2(h2[3]);
+        float4 *o = reinterpret_cast<float4 *>(out) + 2 * (i + u * stride);
+        o[0] = make_float4(a.x, a.y, b.x, b.y);
+        o[1] = make_float4(c.x, c.y, d.x, d.y);
+      }
+    } else {
+      float4 f[U][2];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * stride < chunks) {
+          const float4 *src = reinterpret_cast<const float4 *>(in) + 2 * (i + u * stride);
+          f[u][0] = src[0];
+          f[u][1] = src[1];
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (i + u * stride >= chunks) break;
+        uint4 h;
+        __half2 *h2 = reinterpret_cast<__half2 *>(&h);
+        h2[0] = __floats2half2_rn(f[u][0].x, f[u][0].y);
+        h2[1] = __floats2half2_rn(f[u][0].z, f[u][0].w);
+        h2[2] = __floats2half2_rn(f[u][1].x, f[u][1].y);
+        h2[3] = __floats2half2_rn(f[u][1].z, f[u][1].w);
+        reinterpret_cast<uint4 *>(out)[i + u * stride] = h;
+      }
+    }
+  }
+}
+
 __global__ void cast_kernel(void *__restrict__ out, int to, const void *__restrict__ in, int from, int64_t n) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -177,6 +226,20 @@ extern "C" ipuc_status ipuc_cast(void *out, ipuc_precision to, const void *in, i
   IPUC_CHECK_ARG((to == IPUC_F16 || to == IPUC_F32) && (from == IPUC_F16 || from == IPUC_F32), "cast: bad precision");
   if (element_count == 0) return IPUC_OK;
   IPUC_CHECK_ARG(out && in, "cast: null pointer");
-  cast_kernel<<<grid_for((int64_t)element_count, 256), 256, 0, stream>>>(out, to, in, from, (int64_t)element_count);
+  const int64_t n = (int64_t)element_count;
+  if (to != from && aligned(out, 16) && aligned(in, 16) && n >= 8) {
+    const int64_t chunks = n / 8, done = chunks * 8;
+    if (to == IPUC_F32)
+      cast_vec_kernel<true><<<grid_for(chunks, 256), 256, 0, stream>>>(out, in, chunks);
+    else
+      cast_vec_kernel<false><<<grid_for(chunks, 256), 256, 0, stream>>>(out, in, chunks);
+    if (done < n) {
+      const size_t ob = to == IPUC_F16 ? 2 : 4, ib = from == IPUC_F16 ? 2 : 4;
+      cast_kernel<<<1, 256, 0, stream>>>(static_cast<uint8_t *>(out) + done * ob, to,
+                                         static_cast<const uint8_t *>(in) + done * ib, from, n - done);
+    }
+    return check_launch("cast_vec_kernel");
+  }
+  cast_kernel<<<grid_for(n, 256), 256, 0, stream>>>(out, to, in, from, n);
   return check_launch("cast_kernel");
 }

@@ -65,15 +65,28 @@ def test_add_f16(n, lp, rp):
     assert np.array_equal(host_u16(out), want)
 
 
-def test_cast_round_trip():
-    x = seeded_normal(3, 5000, 100.0)
+@pytest.mark.parametrize("n", [5000, 5003, 7, 1 << 20])
+def test_cast_round_trip(n):
+    """Bit-exact both ways: the 8-element vector path, its scalar tail and
+    short inputs."""
+    x = seeded_normal(3, n, 100.0)
     xd = dev_f32(x)
-    h = empty_u16(5000)
-    ipuc.cast(h, ipuc.F16, xd, ipuc.F32, 5000)
+    h = empty_u16(n)
+    ipuc.cast(h, ipuc.F16, xd, ipuc.F32, n)
     assert np.array_equal(host_u16(h), oracle.f16_bits(x))
-    back = torch.empty(5000, dtype=torch.float32, device="cuda")
-    ipuc.cast(back, ipuc.F32, h, ipuc.F16, 5000)
+    back = torch.empty(n, dtype=torch.float32, device="cuda")
+    ipuc.cast(back, ipuc.F32, h, ipuc.F16, n)
     assert np.array_equal(host_f32(back), oracle.quantize_f16(x))
+
+
+def test_cast_unaligned_views():
+    """Views that start off a 16-byte boundary take the scalar kernel."""
+    n = 1001
+    x = seeded_normal(4, n + 1, 10.0)
+    xd = dev_f32(x)[1:]
+    h = empty_u16(n + 1)[1:]
+    ipuc.cast(h, ipuc.F16, xd, ipuc.F32, n)
+    assert np.array_equal(host_u16(h), oracle.f16_bits(x[1:]))
 
 
 def test_fill_zero():
