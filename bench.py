@@ -792,6 +792,20 @@ def profile_case(kernel: str):
         target = 2 if kernel == "rearrange" else 0
         run = lambda: ipuc.call("ipuc_rearrange_f16", dst.data_ptr(), src.data_ptr(), 1, rows, rows, target, cols,
                                 cols, 64, 16, s)
+    elif kernel in ("reduce", "gelu"):
+        # config 3's unfused stages: split-K reduce of 4 fp32 partials (2.42 GB
+        # on the device) and standalone GELU on the reduced 134M elements
+        cnt = MLP_M * MLP_N
+        parts = torch.randn((4, cnt), device="cuda")
+        y16 = torch.empty(cnt, device="cuda", dtype=torch.float16)
+        if kernel == "reduce":
+            run = lambda: ipuc.call("ipuc_reduce_sum", y16.data_ptr(), parts[0].data_ptr(), parts[1].data_ptr(), 3,
+                                    cnt, ipuc.F32, s)
+        else:
+            del parts
+            y16.normal_()
+            g16 = torch.empty_like(y16)
+            run = lambda: ipuc.call("ipuc_gelu_f16", g16.data_ptr(), y16.data_ptr(), cnt, s)
     else:
         m = n = k = 4096
         a = torch.rand((m, k), device="cuda")
@@ -818,7 +832,7 @@ def main():
                     help="at N>1 every rank uploads all of X in the e2e step (no NVLink all-gather)")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--profile", choices=["gemm", "attention", "attention8", "rearrange", "rearrange_amp_left",
-                                          "gemm_f32"],
+                                          "gemm_f32", "reduce", "gelu"],
                     help="run a few launches of one kernel on a small case (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile:
