@@ -43,7 +43,7 @@ def test_rearrange_block_major_tma_path(matrices, R, C):
 
 
 @pytest.mark.parametrize("order,matrices,R,Rp,C,Cp", [
-    (0, 1, 64, 64, 64, 64), (0, 2, 7, 9, 30, 32), (0, 1, 100, 100, 17, 48),
+    (0, 1, 64, 64, 64, 64), (0, 2, 7, 9, 30, 32), (0, 1, 100, 100, 17, 48), (0, 2, 1000, 1024, 3999, 4096),
     (1, 1, 64, 64, 64, 64), (1, 3, 30, 32, 20, 22), (1, 1, 128, 128, 1, 2),
 ])
 def test_unpack_bit_exact(order, matrices, R, Rp, C, Cp):
