@@ -353,10 +353,7 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (seeded N(0,1) / N(0,1/4096) f16, BASELINE shapes)",
-            "config": {"workload": "config3 MLP up-proj 8192x4096x16384 +GELU fused, N-sharded; config4 flash "
-                                   "attention B=8 H=32 S=4096 D=128, sharded over batch*heads",
-                       "global_batch": MLP_M, "seq_len": ATT_S, "parallelism": f"shard{world}",
-                       "l2": "inputs larger than L2 (no flush)"},
+            "config": step_config(world),
             "gpu_launches": (1 + attention_launches(torch, ns)) * args.steps,
             "clocks": clock_info,
             "e2e": {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -728,6 +725,14 @@ def cpu_baseline(seconds_budget: float):
     return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample}
 
 
+def step_config(world: int) -> dict:
+    """The workload both arms report (config 3 + config 4 of BASELINE.json)."""
+    return {"workload": "config3 MLP up-proj 8192x4096x16384 +GELU fused, N-sharded; config4 flash "
+                        "attention B=8 H=32 S=4096 D=128, sharded over batch*heads",
+            "global_batch": MLP_M, "seq_len": ATT_S, "parallelism": f"shard{world}",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -756,7 +761,8 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "f32 (f16-quantised operands)",
         "data": "synthetic",
-        "config": {"workload": "config3 MLP up-proj + config4 flash attention (reference host evaluator on CPU)"},
+        "config": dict(step_config(args.gpus), evaluator="the reference's host evaluator restated (oracle port), "
+                                                      "on the host cores"),
         "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
