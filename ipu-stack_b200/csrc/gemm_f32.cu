@@ -342,6 +342,11 @@ struct Gemm32Params {
   uint32_t flags;
   uint32_t *err;
   const int32_t *ea, *eb;  // split exponents of the rows of A and the columns of B
+  // Work units of the CTA-pair kernel: units [0, split_from) are whole tiles;
+  // every tile t >= split_from (the last, partial wave) is two units, one per
+  // half of its K chunks, whose epilogues add their partial sums into C
+  // (zeroed beforehand) with atomics.  No split: split_from = num_units = num_tiles.
+  int64_t num_units, split_from;
 };
 
 // C element scale 2^-(e_row + e_col) of the 3xF16 split, exact unless C itself
@@ -360,6 +365,29 @@ __device__ __forceinline__ void tile_coords(const Gemm32Params &p, int64_t t, in
   const int64_t w = t % in_group;
   mt = first + (int)(w % gs);
   nt = (int)(w / gs);
+}
+
+struct WorkUnit {
+  int64_t tile;
+  int c0, c1;   // K chunks [c0, c1)
+  bool split;   // one of two halves: the epilogue adds into C
+};
+__device__ __forceinline__ WorkUnit work_unit(const Gemm32Params &p, int64_t u, int chunks) {
+  if (u < p.split_from) return {u, 0, chunks, false};
+  const int64_t v = u - p.split_from;
+  const int mid = chunks / 2;
+  return {p.split_from + v / 2, (v & 1) ? mid : 0, (v & 1) ? chunks : mid, true};
+}
+
+// Zeroes the C regions of the split tiles (blockIdx.y = tile - split_from).
+__global__ void __launch_bounds__(256) zero_split_tiles_kernel(const Gemm32Params p, int pair_bm) {
+  int mt, nt;
+  tile_coords(p, p.split_from + blockIdx.y, mt, nt);
+  const int64_t r0 = (int64_t)mt * pair_bm, c0 = (int64_t)nt * BN;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < pair_bm * BN; idx += gridDim.x * blockDim.x) {
+    const int64_t r = r0 + idx / BN, c = c0 + idx % BN;
+    if (r < p.m && c < p.n) p.c[r * p.ldc + c] = 0.0f;
+  }
 }
 
 template <bool kF16>
@@ -625,11 +653,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
+      for (int64_t u = pair; u < p.num_units && ok; u += pairs) {
+        const WorkUnit w = work_unit(p, u, chunks);
         int mt, nt;
-        tile_coords(p, t, mt, nt);  // mt counts 256-row pair tiles
+        tile_coords(p, w.tile, mt, nt);  // mt counts 256-row pair tiles
         const int32_t arow = mt * PAIR_BM + (int32_t)rank * BM, brow = nt * BN + (int32_t)rank * (BN / 2);
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int kb_end = min(p.k_blocks, w.c1 * KC);
+        for (int kb = w.c0 * KC; kb < kb_end; ++kb, ++it) {
           const int s = it % P_STAGES;
           const uint32_t ph = (it / P_STAGES) & 1u;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
@@ -656,8 +686,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const uint64_t d0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       uint32_t it = 0, g = 0;
       bool ok = true;
-      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
-        for (int c = 0; c < chunks && ok; ++c, ++g) {
+      for (int64_t u = pair; u < p.num_units && ok; u += pairs) {
+        const WorkUnit w = work_unit(p, u, chunks);
+        for (int c = w.c0; c < w.c1 && ok; ++c, ++g) {
           const uint32_t buf = g & 1u, use = g >> 1;
           if (!mbar_wait_bounded(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
             ok = false;
@@ -705,11 +736,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const bool vec_ok = (p.ldc % 4 == 0);
     uint32_t g = 0;
     bool ok = true;
-    for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
+    for (int64_t u = pair; u < p.num_units && ok; u += pairs) {
+      const WorkUnit w = work_unit(p, u, chunks);
       float acc[BN / 2];
 #pragma unroll
       for (int i = 0; i < BN / 2; ++i) acc[i] = 0.0f;
-      for (int c = 0; c < chunks; ++c, ++g) {
+      for (int c = w.c0; c < w.c1; ++c, ++g) {
         const uint32_t buf = g & 1u, use = g >> 1;
         if (!mbar_wait_bounded(&acc_full[buf], use & 1u, abort_flag)) {
           ok = false;
@@ -730,7 +762,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok) break;
       int mt, nt;
-      tile_coords(p, t, mt, nt);
+      tile_coords(p, w.tile, mt, nt);
       const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
@@ -748,6 +780,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
               v.z = unscale(v.z, er, ec.z);
               v.w = unscale(v.w, er, ec.w);
             }
+            if (w.split) {
+              atomicAdd(c4 + j, v);
+              continue;
+            }
             if (accumulate) {
               const float4 o = c4[j];
               v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
@@ -760,6 +796,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             if (col_base + j < p.n) {
               float x = acc[j];
               if constexpr (kF16) x = unscale(x, er, p.eb[col_base + j]);
+              if (w.split) {
+                atomicAdd(cp + j, x);
+                continue;
+              }
               if (accumulate) x += cp[j];
               cp[j] = x;
             }
@@ -815,6 +855,18 @@ ipuc_status launch_main(const CUtensorMap &tah, const CUtensorMap &tal, void *bh
     p.tiles_m = (int32_t)((m + PAIR_BM - 1) / PAIR_BM);
     p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
     const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
+    // A last wave at most half full runs as two K halves per tile (two units
+    // each), so that it takes about half a wave-time; C must not be an
+    // accumulation target (two atomic adds onto zero are order-independent).
+    const int chunks = (p.k_blocks + Split<kF16>::KC - 1) / Split<kF16>::KC;
+    const int64_t tail = p.num_tiles % pairs;
+    p.split_from = p.num_units = p.num_tiles;
+    if (tail > 0 && 2 * tail <= pairs && chunks >= 2 && !(p.flags & IPUC_GEMM_ACCUMULATE)) {
+      p.split_from = p.num_tiles - tail;
+      p.num_units = p.num_tiles + tail;
+      zero_split_tiles_kernel<<<dim3(16, (unsigned)tail), 256, 0, stream>>>(p, PAIR_BM);
+      if ((st = check_launch("zero_split_tiles_kernel")) != IPUC_OK) return st;
+    }
     IPUC_CUDA(cudaFuncSetAttribute(gemm_split3_pair_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    P_SMEM_BYTES));
     gemm_split3_pair_kernel<kF16><<<(unsigned)(2 * pairs), NUM_THREADS, P_SMEM_BYTES, stream>>>(tah, tal, pbh, pbl, p);
@@ -825,6 +877,7 @@ ipuc_status launch_main(const CUtensorMap &tah, const CUtensorMap &tal, void *bh
   if ((st = make_map_3d(&tbl, dt, eb, bl, k, n, 1, ldp, 0, BK, BN)) != IPUC_OK) return st;
   p.tiles_m = (int32_t)((m + BM - 1) / BM);
   p.num_tiles = (int64_t)p.tiles_m * p.tiles_n;
+  p.split_from = p.num_units = p.num_tiles;
   const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
   IPUC_CUDA(cudaFuncSetAttribute(gemm_split3_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   gemm_split3_kernel<kF16><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tah, tal, tbh, tbl, p);

@@ -127,3 +127,15 @@ def test_gemm_f32_tiny_and_huge_magnitudes():
         s = np.abs(a[r]).astype(np.float64).max() * np.abs(b).max()
         tol = 1e-5 if r != 0 else 1e-3   # a subnormal row carries fewer than 24 bits itself
         assert np.abs(got[r] - ref[r]).max() <= tol * s * np.sqrt(k), r
+
+
+@pytest.mark.parametrize("bt", [False, True])
+@pytest.mark.parametrize("split", SPLITS)
+def test_gemm_f32_split_k_tail(bt, split):
+    """153 pair tiles on 74 CTA pairs leave a last wave of 5 tiles, which runs as
+    two K halves per tile added into C by atomics: the last tile column is 8
+    wide (4104 = 16 * 256 + 8) and the last tile row ragged (2200 rows)."""
+    got, ref, _, _ = run(2200, 4104, 1000, (ipuc.GEMM_B_TRANSPOSED if bt else 0) | split, seed=37)
+    assert rel_l2(got, ref) <= 1e-5
+    again, _, _, _ = run(2200, 4104, 1000, (ipuc.GEMM_B_TRANSPOSED if bt else 0) | split, seed=37)
+    assert np.array_equal(got, again)   # two atomic adds onto zero do not depend on their order
