@@ -8,9 +8,9 @@ the same message from CUDA event timings (Session.profile_capnp, one tile per
 GPU, clockHz 1e9 so a cycle is a nanosecond); `write` encodes any report
 through the library's encoder (ipug_profile_encode) and `read` decodes one
 (any segment count, far pointers included) following the published Cap'n
-Proto encoding.  `merge` joins the one-tile reports of several GPUs, and
-`query` is the group-by summary of ipu-profile's query (count, cycles, ms per
-kernel, operation, kind, tile or phase).
+Proto encoding.  `merge` joins the one-tile reports of several GPUs (`gather`
+across torch.distributed ranks), and `query` is ipu-profile's query: the same
+filters, grouping, ordering and report fields.
 
 Data classes mirror the reference's Rust types: ProfileReport{clock_hz, tiles},
 TileProfile{physical_tile, samples}, CycleSample{step, start_cycle, end_cycle},
@@ -300,16 +300,83 @@ def merge(reports) -> ProfileReport:
     return ProfileReport(clock, [t for r in reports for t in r.tiles])
 
 
-def query(report: ProfileReport, group_by: str = "kernel", kind: str | None = None) -> list:
-    """Rows {name, samples, cycles, ms, tiles} grouped like ipu-profile's
-    query (GroupBy kind/kernel/operation/phase/tile,
-    crates/ipu-profile/src/lib.rs:632-668), sorted by cycles, largest first."""
-    groups = {}
+GROUP_BY = ("kind", "kernel", "operation", "phase", "tile", "metadata")
+SORT_BY = ("phase-cycles", "work-cycles", "maximum-cycles", "samples", "name")
+
+
+def _i32(x: int) -> int:
+    x &= 0xFFFFFFFF
+    return x - (1 << 32) if x >= (1 << 31) else x
+
+
+def _duration(smp: CycleSample) -> int:
+    return (smp.end_cycle - smp.start_cycle) & 0xFFFFFFFF
+
+
+def cycle_origin(report: ProfileReport) -> int:
+    """The common cycle origin of the tiles' first samples on the wrapping
+    32-bit counter (crates/ipu-profile/src/lib.rs:285-299)."""
+    firsts = [t.samples[0].start_cycle for t in report.tiles if t.samples]
+    if not firsts:
+        return 0
+    ref = firsts[0]
+    return (ref + min(_i32(f - ref) for f in firsts)) & 0xFFFFFFFF
+
+
+def _union_length(intervals) -> int:
+    total, cur = 0, None
+    for lo, hi in sorted(intervals):
+        if cur is None:
+            cur = [lo, hi]
+        elif lo <= cur[1]:
+            cur[1] = max(cur[1], hi)
+        else:
+            total += cur[1] - cur[0]
+            cur = [lo, hi]
+    return total + (cur[1] - cur[0] if cur else 0)
+
+
+def query(report: ProfileReport, group_by: str = "kernel", sort_by: str = "phase-cycles", kind: str | None = None,
+          kernel: str | None = None, operation_contains: str | None = None, tiles=(), phases=(), metadata=(),
+          metadata_key: str | None = None, at_offset: int | None = None, shared_clock: bool = False,
+          limit: int | None = None, sample_limit: int = 0) -> dict:
+    """`ipu-profile query` on a report (crates/ipu-profile/src/lib.rs:450-585):
+    the same filters (kind, kernel, operation substring, tiles, phases, metadata
+    name[=value] pairs, a cycle offset the sample must cover), group-by
+    (kind, kernel, operation, phase, tile, metadata value under metadata_key),
+    sort order and limits, and the same report fields in camelCase.  Offsets
+    count from the tiles' common cycle origin; unless shared_clock, the span
+    before the last tile's first sample is cropped.  Per group, phaseCycles is
+    the length of the union of its samples' intervals and workCycles their sum."""
+    if group_by not in GROUP_BY or sort_by not in SORT_BY:
+        raise ValueError(f"group_by one of {GROUP_BY}, sort_by one of {SORT_BY}")
+    tiles, phases = set(tiles), set(phases)
+    metadata = [(m, None) if isinstance(m, str) else tuple(m) for m in metadata]
+    base = cycle_origin(report)
+    crop = 0 if shared_clock else max(
+        (((t.samples[0].start_cycle - base) & 0xFFFFFFFF) for t in report.tiles if t.samples), default=0)
+    sample_count = sum(len(t.samples) for t in report.tiles)
+    span = 0
+    groups, candidates, matched = {}, [], 0
     for tile in report.tiles:
         for smp in tile.samples:
+            raw = (smp.start_cycle - base) & 0xFFFFFFFF
+            raw_end = raw + _duration(smp)
+            span = max(span, max(raw_end - crop, 0))
+            off, end = max(raw - crop, 0), max(raw_end - crop, 0)
+            dur = min(end - off, 0xFFFFFFFF)
             st = smp.step
-            if kind is not None and st.kind != kind:
+            if dur == 0:
                 continue
+            if ((kind is not None and st.kind != kind) or (kernel is not None and st.kernel != kernel)
+                    or (operation_contains is not None and operation_contains not in st.operation)
+                    or (tiles and tile.physical_tile not in tiles) or (phases and st.phase not in phases)
+                    or (at_offset is not None and not off <= at_offset < off + dur)):
+                continue
+            if not all(any(n == name and (v is None or val == v) for n, val in st.metadata) for name, v in metadata):
+                continue
+            matched += 1
+            dims = {}
             if group_by == "kind":
                 name = st.kind
             elif group_by == "kernel":
@@ -317,20 +384,51 @@ def query(report: ProfileReport, group_by: str = "kernel", kind: str | None = No
             elif group_by == "operation":
                 name = st.operation
             elif group_by == "phase":
+                dims = {"phase": str(st.phase), "epoch": str(st.epoch)}
                 name = f"phase {st.phase}/{st.epoch}"
             elif group_by == "tile":
+                dims = {"physicalTile": str(tile.physical_tile)}
                 name = f"tile {tile.physical_tile}"
             else:
-                raise ValueError(f"unknown group_by {group_by!r}")
-            g = groups.setdefault(name, {"name": name, "samples": 0, "cycles": 0, "tiles": set()})
-            g["samples"] += 1
-            g["cycles"] += max(0, smp.end_cycle - smp.start_cycle)
+                key = metadata_key or ""
+                value = next((val for n, val in st.metadata if n == key), "(missing)")
+                dims = {"metadataKey": key, "metadataValue": value}
+                name = value
+            g = groups.setdefault(name, {"dims": dims, "durations": [], "tiles": set(), "phases": set(),
+                                         "intervals": [], "first": off, "last": 0})
+            g["durations"].append(dur)
             g["tiles"].add(tile.physical_tile)
-    rows = sorted(groups.values(), key=lambda g: (-g["cycles"], g["name"]))
-    for g in rows:
-        g["ms"] = g["cycles"] * 1e3 / report.clock_hz if report.clock_hz else 0.0
-        g["tiles"] = sorted(g["tiles"])
-    return rows
+            g["phases"].add((st.phase, st.epoch))
+            g["intervals"].append((off, off + dur))
+            g["first"] = min(g["first"], off)
+            g["last"] = max(g["last"], off + dur)
+            if sample_limit > 0:
+                candidates.append((tile.physical_tile, off, dur, smp))
+    ms = (lambda c: c * 1e3 / report.clock_hz) if report.clock_hz else (lambda c: 0.0)
+    summaries = []
+    for name, g in groups.items():
+        d = sorted(g["durations"])
+        work, phase = sum(d), _union_length(g["intervals"])
+        summaries.append({
+            "name": name, "dimensions": g["dims"], "sampleCount": len(d), "tileCount": len(g["tiles"]),
+            "phaseCount": len(g["phases"]), "phaseCycles": phase, "phaseMs": ms(phase), "workCycles": work,
+            "averageActiveTiles": work / phase if phase else 0.0, "meanCycles": work / len(d),
+            "p50Cycles": d[(len(d) - 1) * 50 // 100], "p95Cycles": d[(len(d) - 1) * 95 // 100],
+            "maximumCycles": d[-1], "firstOffset": g["first"], "lastOffset": g["last"]})
+    primary = {"phase-cycles": lambda s: -s["phaseCycles"], "work-cycles": lambda s: -s["workCycles"],
+               "maximum-cycles": lambda s: -s["maximumCycles"], "samples": lambda s: -s["sampleCount"],
+               "name": lambda s: s["name"]}[sort_by]
+    summaries.sort(key=lambda s: (primary(s), s["firstOffset"], s["name"]))
+    if limit is not None:
+        summaries = summaries[:limit]
+    candidates.sort(key=lambda c: (-c[2], c[0], c[1]))
+    samples = [{"physicalTile": t, "offset": off, "duration": dur, "phase": smp.step.phase,
+                "epoch": smp.step.epoch, "kind": smp.step.kind, "operation": smp.step.operation,
+                "kernel": smp.step.kernel, "metadata": [{"name": n, "value": v} for n, v in smp.step.metadata]}
+               for t, off, dur, smp in candidates[:sample_limit]]
+    return {"clockHz": report.clock_hz, "tileCount": len(report.tiles), "sampleCount": sample_count,
+            "matchedSampleCount": matched, "profileSpanCycles": span, "profileSpanMs": ms(span),
+            "atOffset": at_offset, "groups": summaries, "samples": samples}
 
 
 def gather(data: bytes, group=None, dst: int = 0):

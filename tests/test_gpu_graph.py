@@ -83,8 +83,8 @@ def test_transformer_block_small():
     assert samples[0].start_cycle == 0
     assert all(a.end_cycle <= b.start_cycle + 1 and a.start_cycle <= a.end_cycle for a, b in zip(samples, samples[1:]))
     assert samples[-1].end_cycle > 0
-    top = P.query(rep, "kernel")[0]
-    assert top["samples"] >= 1 and top["ms"] > 0
+    top = P.query(rep, "kernel")["groups"][0]
+    assert top["sampleCount"] >= 1 and top["phaseMs"] > 0
 
 
 def test_attention_without_merge_keeps_split_heads():

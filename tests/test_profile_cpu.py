@@ -10,6 +10,7 @@ lib.rs:229-234).
 """
 import struct
 
+import numpy as np
 import pytest
 
 import ipuc
@@ -156,14 +157,83 @@ def test_merge_and_query():
     r1 = P.ProfileReport(1_000_000_000, [tile(1, [("gemm", 0, 2000), ("attn", 2000, 3000)])])
     m = P.merge([r0, r1])
     assert [t.physical_tile for t in m.tiles] == [0, 1]
-    rows = P.query(m, "kernel")
-    assert [(r["name"], r["samples"], r["cycles"], r["tiles"]) for r in rows] == [
-        ("attn", 2, 4000, [0, 1]), ("gemm", 2, 3000, [0, 1])]
-    assert rows[0]["ms"] == pytest.approx(4e-3)
-    assert [r["name"] for r in P.query(m, "tile")] == ["tile 0", "tile 1"]
-    assert P.query(m, "kernel", kind="idle") == []
+    rep = P.query(m, "kernel", sort_by="work-cycles")
+    assert [(g["name"], g["sampleCount"], g["workCycles"], g["tileCount"]) for g in rep["groups"]] == [
+        ("attn", 2, 4000, 2), ("gemm", 2, 3000, 2)]
+    assert rep["groups"][0]["phaseCycles"] == 3000 and rep["groups"][0]["phaseMs"] == pytest.approx(3e-3)
+    assert rep["sampleCount"] == rep["matchedSampleCount"] == 4 and rep["profileSpanCycles"] == 4000
+    assert [g["name"] for g in P.query(m, "tile", sort_by="name")["groups"]] == ["tile 0", "tile 1"]
+    assert P.query(m, "kernel", kind="idle")["groups"] == []
     with pytest.raises(P.ProfileError):
         P.merge([r0, P.ProfileReport(2, [])])
+
+
+# The query cases below restate the reference's own tests of `ipu-profile query`
+# (crates/ipu-profile/src/lib.rs:792-1049) with their expected values.
+
+def _smp(phase, kind, kernel, start, end):
+    step = P.ProfileStep(phase, phase, 0, f"operation {phase}", kind, kernel, [("block", str(phase))])
+    return P.CycleSample(step, start, end)
+
+
+def test_query_groups_parallel_samples_by_kernel():
+    rep = P.ProfileReport(1_000_000_000, [P.TileProfile(2, [_smp(0, "compute", "add", 100, 120)]),
+                                          P.TileProfile(3, [_smp(1, "compute", "add", 100, 130)])])
+    r = P.query(rep)
+    (g,) = r["groups"]
+    assert (g["phaseCycles"], g["workCycles"], g["averageActiveTiles"]) == (30, 50, 50 / 30)
+    assert r["profileSpanCycles"] == 30
+
+
+def test_query_crops_one_common_initial_entry_span():
+    rng = np.random.default_rng(0x70726F6772616D)
+    for case in range(64):
+        starts = rng.integers(1000, 10001, rng.integers(2, 33))
+        boundary = int(starts.max()) + int(rng.integers(1, 2001))
+        work = int(rng.integers(1, 2001))
+        rep = P.ProfileReport(1_000_000_000, [
+            P.TileProfile(t, [_smp(0, "synchronization", "", int(st), boundary),
+                              _smp(1, "compute", "work", boundary, boundary + work)])
+            for t, st in enumerate(starts)])
+        aligned = P.query(rep, group_by="kind")
+        shared = P.query(rep, shared_clock=True)
+        wait = boundary - int(starts.max())
+        assert aligned["profileSpanCycles"] == wait + work, case
+        assert shared["profileSpanCycles"] >= aligned["profileSpanCycles"], case
+        groups = {g["name"]: g for g in aligned["groups"]}
+        assert groups["synchronization"]["firstOffset"] == 0 and groups["synchronization"]["maximumCycles"] == wait
+        assert groups["compute"]["firstOffset"] == wait
+
+
+def test_query_phase_cycles_of_sequential_repeats():
+    rep = P.ProfileReport(1_000_000_000, [
+        P.TileProfile(2, [_smp(0, "compute", "gemm", 100, 110), _smp(0, "compute", "gemm", 110, 120)]),
+        P.TileProfile(3, [_smp(0, "compute", "gemm", 100, 108), _smp(0, "compute", "gemm", 108, 116)])])
+    g = P.query(rep)["groups"][0]
+    assert (g["phaseCycles"], g["workCycles"], g["averageActiveTiles"]) == (20, 36, 1.8)
+
+
+def test_query_common_origin_keeps_entry_skew_out_of_later_samples():
+    rep = P.ProfileReport(1_000_000_000, [
+        P.TileProfile(2, [_smp(0, "exchange", "", 100, 150), _smp(1, "compute", "gemm", 150, 160)]),
+        P.TileProfile(3, [_smp(0, "exchange", "", 120, 150), _smp(1, "compute", "gemm", 150, 160)])])
+    r = P.query(rep, kind="compute", sample_limit=2, shared_clock=True)
+    assert len(r["samples"]) == 2 and all(x["offset"] == 50 for x in r["samples"])
+    assert r["groups"][0]["phaseCycles"] == 10
+
+
+def test_query_time_and_metadata_filters_across_counter_wrap():
+    rep = P.ProfileReport(1_500_000_000, [P.TileProfile(9, [_smp(0, "exchange", "", 0xFFFFFFFF - 4, 5),
+                                                            _smp(1, "compute", "add", 5, 15)])])
+    r = P.query(rep, at_offset=12, metadata=[("block", "1")], sample_limit=1)
+    assert r["matchedSampleCount"] == 1 and r["samples"][0]["phase"] == 1 and r["samples"][0]["offset"] == 10
+
+
+def test_query_groups_by_metadata_value():
+    rep = P.ProfileReport(1_000_000_000, [P.TileProfile(1, [_smp(0, "compute", "add", 0, 10),
+                                                            _smp(1, "compute", "add", 10, 30)])])
+    r = P.query(rep, group_by="metadata", metadata_key="block")
+    assert [g["name"] for g in r["groups"]] == ["1", "0"]
 
 
 def _gather_worker(rank, world, port, out):
@@ -204,4 +274,4 @@ def test_gather_across_gloo_ranks():
         assert p.exitcode == 0
     rep = P.read(data)
     assert [t.physical_tile for t in rep.tiles] == [0, 1]
-    assert [r["name"] for r in P.query(rep, "kernel")] == ["gemm_rank1", "gemm_rank0"]
+    assert [g["name"] for g in P.query(rep, "kernel")["groups"]] == ["gemm_rank1", "gemm_rank0"]
