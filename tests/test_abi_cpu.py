@@ -59,6 +59,41 @@ def test_validation_rejects_before_launch(fn, args, status, text):
     assert text in L.ipuc_last_error_string().decode()
 
 
+FAKE = 1 << 20   # a 256-byte aligned address that validation rejects the call before touching
+
+
+@pytest.mark.parametrize("args,status,text", [
+    ((FAKE, FAKE, FAKE, 64, 64, 64, 64, 64, 64, ipuc.GEMM_OUT_F32, FAKE, 1 << 30, None), ipuc.ERR_INVALID_ARGUMENT,
+     "only IPUC_GEMM_ACCUMULATE"),
+    ((FAKE, FAKE, FAKE, 64, 64, 62, 62, 64, 64, 0, FAKE, 1 << 30, None), ipuc.ERR_ALIGNMENT, "multiples of 4"),
+    ((FAKE, FAKE, FAKE, 64, 64, 64, 64, 64, 64, ipuc.GEMM_F32_SPLIT_TF32, None, 0, None), ipuc.ERR_INVALID_ARGUMENT,
+     "workspace smaller"),
+    ((FAKE, FAKE, FAKE, 64, 64, 64, 64, 64, 64, 0, FAKE, 16, None), ipuc.ERR_INVALID_ARGUMENT, "workspace smaller"),
+])
+def test_gemm_f32_validation(args, status, text):
+    L = ipuc.lib()
+    assert L.ipuc_gemm_f32(*args) == status
+    assert text in L.ipuc_last_error_string().decode()
+
+
+def test_gemm_f32_workspace_covers_both_splits():
+    for m, n, k in [(1, 4, 4), (300, 260, 100), (4096, 4096, 4096), (2200, 4104, 1000)]:
+        kp = (k + 7) // 8 * 8
+        r = lambda x: (x + 255) // 256 * 256
+        f16 = 2 * r(m * kp * 2) + 2 * r(n * kp * 2) + r(m * 4) + 2 * r(n * 4)
+        tf32 = 2 * r(m * k * 4) + 2 * r(k * n * 4)
+        assert ipuc.gemm_f32_workspace_bytes(m, n, k) == max(f16, tf32)
+
+
+def test_graph_library_exports_every_ipug_symbol():
+    text = re.sub(r"/\*.*?\*/", "", open(os.path.join(ROOT, "include", "ipug.h")).read(), flags=re.S)
+    names = sorted(set(re.findall(r"\b(ipug_[a-z0-9_]+)\s*\(", text)))
+    assert len(names) >= 15
+    L = ipuc.lib()
+    for name in names:
+        assert hasattr(L, name), name
+
+
 def test_ipuc_error_carries_status():
     with pytest.raises(ipuc.IpucError) as e:
         ipuc.call("ipuc_gelu_f16", None, None, 5, None)
