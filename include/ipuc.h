@@ -127,9 +127,14 @@ ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t
 /* Replaces ipu_stack_gemm_f32_{init,accumulate}_* (device/gemm_f32_64_amp.S:
  * 129-385).  f32 in, f32 out, C (+)= A.B on the tensor cores with a
  * three-pass f16 split (each row of A and column of B scaled by a power of
- * two, then x = hi + lo in f16; hi.hi + hi.lo + lo.hi in fp32), accurate to
- * an f32 tolerance relative to each row's and column's own magnitude.
- * Non-finite inputs make the affected rows and columns NaN.
+ * two, then x = hi + lo in f16; hi.hi + hi.lo + lo.hi in fp32).  Elements
+ * more than 2^17 below their row's or column's largest magnitude keep fewer
+ * bits in that split; every C element whose value those elements (or an
+ * inf/NaN input) could have moved beyond 2^-23 of itself is recomputed with
+ * fp32 FMAs instead, so results hold an fp32 tolerance element by element
+ * for any input, and non-finite inputs give the IEEE result per element.
+ * (The IPUC_GEMM_F32_SPLIT_TF32 split keeps 22 bits per element by itself,
+ * but an inf/NaN input there turns its whole row/column of C NaN.)
  * workspace: caller-provided device scratch of ipuc_gemm_f32_workspace_bytes()
  * bytes (the hi/lo split operands), 256-byte aligned.  Requirements:
  * 16-byte aligned pointers; k, n, lda and ldb multiples of 4 elements.
@@ -149,16 +154,20 @@ ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, int64_t m, i
  * the split planes live in a fixed 64 MiB file-scope device array of
  * libipuc.so instead.  Arguments, flags and results are exactly those
  * of ipuc_gemm_f32 without the workspace pair.
- *  - Limit: 4 * (m + n) * kp + 4 * m + 8 * n bytes (kp = k rounded up to 8,
- *    each of the seven arrays rounded up to 256 bytes) <= 64 MiB (e.g.
- *    m = n = k = 2880); with IPUC_GEMM_F32_SPLIT_TF32, 8 * (m + n) * k bytes
+ *  - Limit: 4 * (m + n) * kp + 12 * (m + n) + 4 * m * ceil(n / 32) bytes
+ *    (kp = k rounded up to 8, each of the eleven arrays rounded up to 256
+ *    bytes) <= 64 MiB (e.g. m = n = k = 2864); with
+ *    IPUC_GEMM_F32_SPLIT_TF32, 8 * (m + n) * k bytes
  *    (e.g. m = n = k = 2048); larger
  *    shapes return IPUC_ERR_INVALID_ARGUMENT and launch nothing.
  *  - Allocates nothing: no cudaMalloc/cudaFree and no allocating library call.
  *    The array exists on every GPU that loads the library, until process exit.
  *  - The first call on each device resolves the array's device address with
  *    cudaGetSymbolAddress (with that device current); make that first call
- *    before any stream capture on the device.
+ *    before any stream capture on the device.  The address is cached with the
+ *    context it was resolved in: after cudaDeviceReset, or when the caller
+ *    makes another context current on the device, the next call resolves it
+ *    again (so that call, too, belongs before any capture).
  *  - Every call shares the one array: calls that overlap on the GPU (two
  *    streams, or concurrent host threads) race.  Nothing in it needs clearing
  *    between calls. */

@@ -149,7 +149,22 @@ __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float *
 // row's maximum (smaller ones keep an absolute error below 2^-39 of it), and
 // the MMA products of the scaled planes equal the TF32 split's to the bit
 // budget.  The epilogue multiplies C by 2^-(e_row + e_col).  Maxima are kept
-// as float bits (non-negative floats order like their bit patterns).
+// as the bits of |x| compared as integers: non-negative floats order like
+// their bit patterns, and +inf and NaN sort above every finite value, so a
+// maximum >= 0x7f800000 marks a row or column holding a non-finite value.
+//
+// Elements more than 2^17 below their row's (column's) maximum keep fewer
+// than 22 bits (their lo part falls into f16 subnormals).  The prepass counts
+// them per row and column ("tiny" counts; a non-finite row or column gets
+// kTinyAll).  With T tiny elements in row i and column j together, the lost
+// bits add at most T * 2^-10 to the scaled product sum C_s (each such operand
+// is off by at most 2^-25 and its partner is below 2^15).  The epilogue keeps
+// C_s only where that bound is below 2^-23 |C_s|; otherwise it leaves the
+// element alone and marks it in a bitmap, and a fix-up kernel recomputes the
+// marked elements with plain fp32 FMAs from A and B (which also gives the
+// IEEE inf/NaN pattern of a non-finite input element by element).  Rows of
+// everyday data (normal or uniform values, K in the thousands) hold at most a
+// few tiny elements and mark nothing or next to nothing.
 
 // e such that mx * 2^e lies in [2^14, 2^15); 0 for zero, inf and NaN rows;
 // at most 126 so that 2^e and 2^-e are normal floats.
@@ -168,6 +183,17 @@ __host__ __device__ __forceinline__ int split_exponent(uint32_t max_bits) {
 
 __device__ __forceinline__ float pow2(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
 
+constexpr int32_t kTinyAll = 1 << 24;           // tiny count of a row/column with a non-finite value
+__device__ __forceinline__ uint32_t abs_bits(float x) { return __float_as_uint(x) & 0x7fffffffu; }
+// A scaled element that keeps fewer than 22 bits in hi + lo.
+__device__ __forceinline__ int is_tiny(float xs) { return xs != 0.0f && fabsf(xs) < 0.125f; }
+// True where the tiny elements of the element's row and column (`tiny`
+// together) may have moved the scaled sum v by more than 2^-23 |v| (or v is
+// not finite while a non-finite input is involved).
+__device__ __forceinline__ bool needs_fixup(float v, int tiny) {
+  return tiny != 0 && !(fabsf(v) * 0x1p-13f >= (float)tiny);
+}
+
 __device__ __forceinline__ void split_f16(float x, float scale, __half &h, __half &l) {
   const float xs = x * scale;
   h = __float2half_rn(xs);
@@ -182,13 +208,13 @@ __device__ __forceinline__ void split_f16(float x, float scale, __half &h, __hal
 constexpr int COLMAX_ROWS = 128;
 __global__ void __launch_bounds__(256) col_absmax_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                          int64_t ld, uint32_t *__restrict__ out) {
-  __shared__ float4 part[8][32];
+  __shared__ uint4 part[8][32];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int64_t col_tiles = (cols + 127) / 128, bands = (rows + COLMAX_ROWS - 1) / COLMAX_ROWS;
   for (int64_t t = blockIdx.x; t < col_tiles * bands; t += gridDim.x) {
     const int64_t c = (t % col_tiles) * 128 + 4 * tx;
     const int64_t r0 = (t / col_tiles) * COLMAX_ROWS, r1 = min(rows, r0 + COLMAX_ROWS);
-    float4 mx = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    uint4 mx = make_uint4(0u, 0u, 0u, 0u);
     if (c < cols) {
       for (int64_t r = r0 + ty; r < r1; r += 32) {
         float4 v[4];
@@ -198,8 +224,8 @@ __global__ void __launch_bounds__(256) col_absmax_kernel(const float *__restrict
                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          mx.x = fmaxf(mx.x, fabsf(v[u].x)); mx.y = fmaxf(mx.y, fabsf(v[u].y));
-          mx.z = fmaxf(mx.z, fabsf(v[u].z)); mx.w = fmaxf(mx.w, fabsf(v[u].w));
+          mx.x = max(mx.x, abs_bits(v[u].x)); mx.y = max(mx.y, abs_bits(v[u].y));
+          mx.z = max(mx.z, abs_bits(v[u].z)); mx.w = max(mx.w, abs_bits(v[u].w));
         }
       }
     }
@@ -209,13 +235,13 @@ __global__ void __launch_bounds__(256) col_absmax_kernel(const float *__restrict
     if (ty == 0 && c < cols) {
 #pragma unroll
       for (int y = 1; y < 8; ++y) {
-        const float4 o = part[y][tx];
-        mx.x = fmaxf(mx.x, o.x); mx.y = fmaxf(mx.y, o.y); mx.z = fmaxf(mx.z, o.z); mx.w = fmaxf(mx.w, o.w);
+        const uint4 o = part[y][tx];
+        mx.x = max(mx.x, o.x); mx.y = max(mx.y, o.y); mx.z = max(mx.z, o.z); mx.w = max(mx.w, o.w);
       }
-      atomicMax(out + c, __float_as_uint(mx.x));
-      atomicMax(out + c + 1, __float_as_uint(mx.y));
-      atomicMax(out + c + 2, __float_as_uint(mx.z));
-      atomicMax(out + c + 3, __float_as_uint(mx.w));
+      atomicMax(out + c, mx.x);
+      atomicMax(out + c + 1, mx.y);
+      atomicMax(out + c + 2, mx.z);
+      atomicMax(out + c + 3, mx.w);
     }
   }
 }
@@ -230,13 +256,15 @@ __global__ void __launch_bounds__(256) col_absmax_kernel(const float *__restrict
 constexpr int ROW_CACHE = 4;
 __global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                              int64_t ld, int32_t *__restrict__ rexp, int64_t ldp,
-                                                             __half *__restrict__ hi, __half *__restrict__ lo) {
-  __shared__ float red[8];
+                                                             __half *__restrict__ hi, __half *__restrict__ lo,
+                                                             int32_t *__restrict__ tiny) {
+  __shared__ uint32_t red[8];
+  __shared__ int cnt[8];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int64_t q = cols / 4, qp = ldp / 4;
   const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  auto amax4 = [](float m, float4 x) {
-    return fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+  auto amax4 = [](uint32_t m, float4 x) {
+    return max(max(m, max(abs_bits(x.x), abs_bits(x.y))), max(abs_bits(x.z), abs_bits(x.w)));
   };
   auto put = [&](int64_t r, int64_t c, float4 x, float scale) {
     __half h[4], l[4];
@@ -246,11 +274,12 @@ __global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__rest
     split_f16(x.w, scale, h[3], l[3]);
     *reinterpret_cast<uint2 *>(hi + r * ldp + 4 * c) = *reinterpret_cast<const uint2 *>(h);
     *reinterpret_cast<uint2 *>(lo + r * ldp + 4 * c) = *reinterpret_cast<const uint2 *>(l);
+    return is_tiny(x.x * scale) + is_tiny(x.y * scale) + is_tiny(x.z * scale) + is_tiny(x.w * scale);
   };
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float4 *row = reinterpret_cast<const float4 *>(src + r * ld);
     float4 v[ROW_CACHE];
-    float mx = 0.0f;
+    uint32_t mx = 0;
 #pragma unroll
     for (int u = 0; u < ROW_CACHE; ++u) {
       const int64_t c = tid + u * 256;
@@ -259,22 +288,33 @@ __global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__rest
     }
     for (int64_t c = tid + ROW_CACHE * 256; c < q; c += 256) mx = amax4(mx, row[c]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if (lane == 0) red[wid] = mx;
     __syncthreads();
     mx = red[0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
-    __syncthreads();  // red is rewritten for the next row
-    const int e = split_exponent(__float_as_uint(mx));
+    for (int w = 1; w < 8; ++w) mx = max(mx, red[w]);
+    const int e = split_exponent(mx);
     if (tid == 0) rexp[r] = e;
     const float scale = pow2(e);
+    int t = 0;
 #pragma unroll
     for (int u = 0; u < ROW_CACHE; ++u) {
       const int64_t c = tid + u * 256;
-      if (c < qp) put(r, c, v[u], scale);
+      if (c < qp) t += put(r, c, v[u], scale);
     }
-    for (int64_t c = tid + ROW_CACHE * 256; c < qp; c += 256) put(r, c, c < q ? row[c] : zero, scale);
+    for (int64_t c = tid + ROW_CACHE * 256; c < qp; c += 256) t += put(r, c, c < q ? row[c] : zero, scale);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) cnt[wid] = t;
+    __syncthreads();
+    if (tid == 0) {
+      int total = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) total += cnt[w];
+      tiny[r] = mx >= 0x7f800000u ? kTinyAll : total;
+    }
+    __syncthreads();  // red and cnt are rewritten for the next row
   }
 }
 
@@ -289,7 +329,7 @@ __global__ void __launch_bounds__(256) split_f16_transpose_kernel(const float *_
                                                                   int64_t cols, int64_t ld,
                                                                   const uint32_t *__restrict__ cmax, int64_t ldp,
                                                                   __half *__restrict__ hi, __half *__restrict__ lo,
-                                                                  int32_t *__restrict__ cexp) {
+                                                                  int32_t *__restrict__ cexp, int32_t *__restrict__ tiny) {
   __shared__ float tile[64][65];
   const int64_t tr = (ldp + 63) / 64, tc = (cols + 63) / 64;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -320,15 +360,30 @@ __global__ void __launch_bounds__(256) split_f16_transpose_kernel(const float *_
     for (int i = 0; i < 4; ++i) {
       const int oc = ty + 16 * i, orr = tx * 4;  // plane row = source column c0 + oc
       const int64_t c = c0 + oc, r = r0 + orr;
-      if (c >= cols || r >= ldp) continue;
-      const int ce = split_exponent(cmax[c]);
-      if (r0 == 0 && tx == 0) cexp[c] = ce;
-      const float scale = pow2(ce);
-      __half h[4], l[4];
+      int t = 0;
+      if (c < cols && r < ldp) {
+        const uint32_t mx = cmax[c];
+        const int ce = split_exponent(mx);
+        if (r0 == 0 && tx == 0) {
+          cexp[c] = ce;
+          if (mx >= 0x7f800000u) tiny[c] = kTinyAll;
+        }
+        const float scale = pow2(ce);
+        __half h[4], l[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) split_f16(tile[orr + e][oc], scale, h[e], l[e]);
-      *reinterpret_cast<uint2 *>(hi + c * ldp + r) = *reinterpret_cast<const uint2 *>(h);
-      *reinterpret_cast<uint2 *>(lo + c * ldp + r) = *reinterpret_cast<const uint2 *>(l);
+        for (int e = 0; e < 4; ++e) {
+          const float x = tile[orr + e][oc];
+          split_f16(x, scale, h[e], l[e]);
+          t += is_tiny(x * scale);
+        }
+        *reinterpret_cast<uint2 *>(hi + c * ldp + r) = *reinterpret_cast<const uint2 *>(h);
+        *reinterpret_cast<uint2 *>(lo + c * ldp + r) = *reinterpret_cast<const uint2 *>(l);
+        if (mx >= 0x7f800000u) t = 0;  // the column is marked whole
+      }
+      // the 16 threads of a half-warp share the plane row c
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (tx == 0 && t > 0) atomicAdd(tiny + c, t);
     }
   }
 }
@@ -342,6 +397,10 @@ struct Gemm32Params {
   uint32_t flags;
   uint32_t *err;
   const int32_t *ea, *eb;  // split exponents of the rows of A and the columns of B
+  const int32_t *ta, *tb;  // tiny counts of the rows of A and the columns of B
+  uint32_t *fixmap;        // [m][fix_words] bitmap of C elements left to the fix-up kernel
+  uint32_t *fixrow;        // [m] nonzero where a row has a marked element
+  int64_t fix_words;
   // Work units of the CTA-pair kernel: units [0, split_from) are whole tiles;
   // every tile t >= split_from (the last, partial wave) is two units, one per
   // half of its K chunks, whose epilogues add their partial sums into C
@@ -355,6 +414,65 @@ __device__ __forceinline__ float unscale(float v, int e_row, int e_col) {
   const int e = e_row + e_col;
   if (e >= -126 && e <= 126) return v * pow2(-e);
   return (v * pow2(-e_row)) * pow2(-e_col);
+}
+
+__device__ __forceinline__ void mark_fixup(const Gemm32Params &p, int64_t row, int64_t col) {
+  atomicOr(p.fixmap + row * p.fix_words + (col >> 5), 1u << (col & 31));
+  p.fixrow[row] = 1u;
+}
+
+// Epilogue store of the scaled sums v of C[row][col .. col+3] (cp points at
+// C[row][col]): unscaled (3xF16), then added atomically (a K-split half),
+// added to C (IPUC_GEMM_ACCUMULATE) or stored; elements that need the fix-up
+// are left alone and marked.
+template <bool kF16>
+__device__ __forceinline__ void store_c4(const Gemm32Params &p, float *cp, int64_t row, int64_t col, float4 v, int er,
+                                         int tr, bool split, bool accumulate) {
+  if constexpr (kF16) {
+    const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col));
+    const int4 tc = __ldg(reinterpret_cast<const int4 *>(p.tb + col));
+    const bool f0 = needs_fixup(v.x, tr + tc.x), f1 = needs_fixup(v.y, tr + tc.y);
+    const bool f2 = needs_fixup(v.z, tr + tc.z), f3 = needs_fixup(v.w, tr + tc.w);
+    v.x = unscale(v.x, er, ec.x);
+    v.y = unscale(v.y, er, ec.y);
+    v.z = unscale(v.z, er, ec.z);
+    v.w = unscale(v.w, er, ec.w);
+    if (f0 | f1 | f2 | f3) {
+      const float x[4] = {v.x, v.y, v.z, v.w};
+      const bool f[4] = {f0, f1, f2, f3};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (f[e]) mark_fixup(p, row, col + e);
+        else if (split) atomicAdd(cp + e, x[e]);
+        else cp[e] = accumulate ? cp[e] + x[e] : x[e];
+      }
+      return;
+    }
+  }
+  float4 *c4 = reinterpret_cast<float4 *>(cp);
+  if (split) {
+    atomicAdd(c4, v);
+    return;
+  }
+  if (accumulate) {
+    const float4 o = *c4;
+    v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+  }
+  *c4 = v;
+}
+
+template <bool kF16>
+__device__ __forceinline__ void store_c1(const Gemm32Params &p, float *cp, int64_t row, int64_t col, float x, int er,
+                                         int tr, bool split, bool accumulate) {
+  if constexpr (kF16) {
+    if (needs_fixup(x, tr + p.tb[col])) {
+      mark_fixup(p, row, col);
+      return;
+    }
+    x = unscale(x, er, p.eb[col]);
+  }
+  if (split) atomicAdd(cp, x);
+  else *cp = accumulate ? *cp + x : x;
 }
 
 __device__ __forceinline__ void tile_coords(const Gemm32Params &p, int64_t t, int &mt, int &nt) {
@@ -552,36 +670,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int64_t row = (int64_t)mt * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
-        const int er = kF16 ? p.ea[row] : 0;
+        const int er = kF16 ? p.ea[row] : 0, tr = kF16 ? p.ta[row] : 0;
         float *cp = p.c + row * p.ldc + col_base;
         if (vec_ok && col_base + BN / 2 <= p.n) {
-          float4 *c4 = reinterpret_cast<float4 *>(cp);
 #pragma unroll
-          for (int j = 0; j < BN / 8; ++j) {
-            float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-            if constexpr (kF16) {
-              const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col_base) + j);
-              v.x = unscale(v.x, er, ec.x);
-              v.y = unscale(v.y, er, ec.y);
-              v.z = unscale(v.z, er, ec.z);
-              v.w = unscale(v.w, er, ec.w);
-            }
-            if (accumulate) {
-              const float4 o = c4[j];
-              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-            }
-            c4[j] = v;
-          }
+          for (int j = 0; j < BN / 8; ++j)
+            store_c4<kF16>(p, cp + 4 * j, row, col_base + 4 * j,
+                           make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]), er, tr, false,
+                           accumulate);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 2; ++j) {
-            if (col_base + j < p.n) {
-              float x = acc[j];
-              if constexpr (kF16) x = unscale(x, er, p.eb[col_base + j]);
-              if (accumulate) x += cp[j];
-              cp[j] = x;
-            }
-          }
+          for (int j = 0; j < BN / 2; ++j)
+            if (col_base + j < p.n) store_c1<kF16>(p, cp + j, row, col_base + j, acc[j], er, tr, false, accumulate);
         }
       }
     }
@@ -766,44 +866,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
       if (row < p.m) {
-        const int er = kF16 ? p.ea[row] : 0;
+        const int er = kF16 ? p.ea[row] : 0, tr = kF16 ? p.ta[row] : 0;
         float *cp = p.c + row * p.ldc + col_base;
         if (vec_ok && col_base + BN / 2 <= p.n) {
-          float4 *c4 = reinterpret_cast<float4 *>(cp);
 #pragma unroll
-          for (int j = 0; j < BN / 8; ++j) {
-            float4 v = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
-            if constexpr (kF16) {
-              const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col_base) + j);
-              v.x = unscale(v.x, er, ec.x);
-              v.y = unscale(v.y, er, ec.y);
-              v.z = unscale(v.z, er, ec.z);
-              v.w = unscale(v.w, er, ec.w);
-            }
-            if (w.split) {
-              atomicAdd(c4 + j, v);
-              continue;
-            }
-            if (accumulate) {
-              const float4 o = c4[j];
-              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-            }
-            c4[j] = v;
-          }
+          for (int j = 0; j < BN / 8; ++j)
+            store_c4<kF16>(p, cp + 4 * j, row, col_base + 4 * j,
+                           make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]), er, tr, w.split,
+                           accumulate);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 2; ++j) {
-            if (col_base + j < p.n) {
-              float x = acc[j];
-              if constexpr (kF16) x = unscale(x, er, p.eb[col_base + j]);
-              if (w.split) {
-                atomicAdd(cp + j, x);
-                continue;
-              }
-              if (accumulate) x += cp[j];
-              cp[j] = x;
-            }
-          }
+          for (int j = 0; j < BN / 2; ++j)
+            if (col_base + j < p.n)
+              store_c1<kF16>(p, cp + j, row, col_base + j, acc[j], er, tr, w.split, accumulate);
         }
       }
     }
@@ -823,10 +898,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 inline uint64_t round256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
+// Recomputes the C elements the 3xF16 epilogue marked (tiny or non-finite
+// operands, see above) as plain fp32 FMA dot products over k, in k order:
+// C = (IPUC_GEMM_ACCUMULATE ? C : 0) + sum_k A[r][k] B[k][j].  One CTA per row
+// with a marked element (grid-stride over the rows; unmarked rows cost one
+// load), threads over the row's columns.
+__global__ void __launch_bounds__(256) gemm_f32_fixup_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                                                             float *__restrict__ c, int64_t m, int64_t n, int64_t k,
+                                                             int64_t lda, int64_t ldb, int64_t ldc, int bt,
+                                                             int accumulate, const uint32_t *__restrict__ fixmap,
+                                                             const uint32_t *__restrict__ fixrow, int64_t words) {
+  for (int64_t r = blockIdx.x; r < m; r += gridDim.x) {
+    if (fixrow[r] == 0) continue;
+    const uint32_t *map = fixmap + r * words;
+    const float *ar = a + r * lda;
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+      if (!((map[j >> 5] >> (j & 31)) & 1u)) continue;
+      float sum = 0.0f;
+      if (bt) {
+        const float *bc = b + j * ldb;
+        for (int64_t q = 0; q < k; ++q) sum = fmaf(ar[q], bc[q], sum);
+      } else {
+        for (int64_t q = 0; q < k; ++q) sum = fmaf(ar[q], b[q * ldb + j], sum);
+      }
+      float *cp = c + r * ldc + j;
+      *cp = accumulate ? *cp + sum : sum;
+    }
+  }
+}
+
 // Workspace, 3xF16: A_hi, A_lo [m x kp] and B_hi, B_lo [n x kp] f16 (kp = k
 // rounded up to 8, so that plane rows are 16-byte multiples for TMA), then the
-// split exponents of A's rows [m] and B's columns [n] (int32) and B's column
-// maxima [n] (u32 float bits, row-major B only), each 256-byte aligned.
+// split exponents of A's rows [m] and B's columns [n] (int32), B's column
+// maxima [n] (u32 |x| bits, row-major B only), the tiny counts of B's columns
+// [n] and A's rows [m], the fix-up row flags [m] and the fix-up bitmap
+// [m x ceil(n / 32)] (u32), each 256-byte aligned.
 // 3xTF32: A_hi, A_lo [m x k] and B_hi, B_lo [n x k] fp32.  The workspace size
 // is the larger of the two.
 int64_t f16_pitch(int64_t k) { return (k + 7) & ~int64_t(7); }
@@ -891,8 +997,9 @@ uint64_t gemm_f32_workspace_for(int64_t m, int64_t n, int64_t k, uint32_t flags)
   if (m <= 0 || n <= 0 || k <= 0) return 0;
   if (flags & IPUC_GEMM_F32_SPLIT_TF32) return tf32_workspace(m, n, k);
   const uint64_t kp = (uint64_t)f16_pitch(k);
-  return 2 * round256((uint64_t)m * kp * 2) + 2 * round256((uint64_t)n * kp * 2) + round256((uint64_t)m * 4) +
-         2 * round256((uint64_t)n * 4);
+  const uint64_t words = ((uint64_t)n + 31) / 32;
+  return 2 * round256((uint64_t)m * kp * 2) + 2 * round256((uint64_t)n * kp * 2) + 3 * round256((uint64_t)m * 4) +
+         3 * round256((uint64_t)n * 4) + round256((uint64_t)m * words * 4);
 }
 
 // ipuc_gemm_f32_workspace_bytes: enough for either split.
@@ -929,7 +1036,9 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
   p.ldc = ldc;
   p.flags = flags;
   p.err = device_error_word();
-  p.ea = p.eb = nullptr;
+  p.ea = p.eb = p.ta = p.tb = nullptr;
+  p.fixmap = p.fixrow = nullptr;
+  p.fix_words = 0;
   ipuc_status st;
   CUtensorMap tah, tal;
 
@@ -941,19 +1050,26 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
     __half *bh = reinterpret_cast<__half *>(bbase);
     __half *bl = reinterpret_cast<__half *>(bbase + round256((uint64_t)n * kp * 2));
     uint8_t *mbase = bbase + 2 * round256((uint64_t)n * kp * 2);
+    const uint64_t m4 = round256((uint64_t)m * 4), n4 = round256((uint64_t)n * 4);
+    const int64_t words = (n + 31) / 32;
     int32_t *ea = reinterpret_cast<int32_t *>(mbase);
-    int32_t *eb = reinterpret_cast<int32_t *>(mbase + round256((uint64_t)m * 4));
-    uint32_t *bmax = reinterpret_cast<uint32_t *>(mbase + round256((uint64_t)m * 4) + round256((uint64_t)n * 4));
-    split_f16_rows_kernel<<<(unsigned)(m < cap ? m : cap), 256, 0, stream>>>(a, m, k, lda, ea, kp, ah, al);
+    int32_t *eb = reinterpret_cast<int32_t *>(mbase + m4);
+    uint32_t *bmax = reinterpret_cast<uint32_t *>(mbase + m4 + n4);
+    int32_t *tb = reinterpret_cast<int32_t *>(mbase + m4 + 2 * n4);  // right after bmax: one memset clears both
+    int32_t *ta = reinterpret_cast<int32_t *>(mbase + m4 + 3 * n4);
+    uint32_t *fixrow = reinterpret_cast<uint32_t *>(mbase + 2 * m4 + 3 * n4);
+    uint32_t *fixmap = reinterpret_cast<uint32_t *>(mbase + 3 * m4 + 3 * n4);
+    IPUC_CUDA(cudaMemsetAsync(fixrow, 0, m4 + round256((uint64_t)m * words * 4), stream));
+    split_f16_rows_kernel<<<(unsigned)(m < cap ? m : cap), 256, 0, stream>>>(a, m, k, lda, ea, kp, ah, al, ta);
     if (bt) {
-      split_f16_rows_kernel<<<(unsigned)(n < cap ? n : cap), 256, 0, stream>>>(b, n, k, ldb, eb, kp, bh, bl);
+      split_f16_rows_kernel<<<(unsigned)(n < cap ? n : cap), 256, 0, stream>>>(b, n, k, ldb, eb, kp, bh, bl, tb);
     } else {
-      IPUC_CUDA(cudaMemsetAsync(bmax, 0, (size_t)n * 4, stream));
+      IPUC_CUDA(cudaMemsetAsync(bmax, 0, 2 * n4, stream));
       const int64_t col_ctas = ((n + 127) / 128) * ((k + COLMAX_ROWS - 1) / COLMAX_ROWS);
       col_absmax_kernel<<<(unsigned)(col_ctas < cap ? col_ctas : cap), 256, 0, stream>>>(b, k, n, ldb, bmax);
       const int64_t tiles = ((kp + 63) / 64) * ((n + 63) / 64);
       split_f16_transpose_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(b, k, n, ldb, bmax, kp,
-                                                                                            bh, bl, eb);
+                                                                                            bh, bl, eb, tb);
     }
     if ((st = check_launch("gemm_f32 split (3xF16)")) != IPUC_OK) return st;
     const auto f16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -961,7 +1077,15 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
     if ((st = make_map_3d(&tal, f16, 2, al, k, m, 1, kp, 0, Split<true>::BK, BM)) != IPUC_OK) return st;
     p.ea = ea;
     p.eb = eb;
-    return launch_main<true>(tah, tal, bh, bl, m, n, k, kp, p, stream);
+    p.ta = ta;
+    p.tb = tb;
+    p.fixmap = fixmap;
+    p.fixrow = fixrow;
+    p.fix_words = words;
+    if ((st = launch_main<true>(tah, tal, bh, bl, m, n, k, kp, p, stream)) != IPUC_OK) return st;
+    gemm_f32_fixup_kernel<<<(unsigned)(m < cap ? m : cap), 256, 0, stream>>>(
+        a, b, c, m, n, k, lda, ldb, ldc, bt ? 1 : 0, (flags & IPUC_GEMM_ACCUMULATE) ? 1 : 0, fixmap, fixrow, words);
+    return check_launch("gemm_f32_fixup_kernel");
   }
 
   // 3xTF32: unscaled TF32 hi/lo planes, fp32 storage.
@@ -1013,7 +1137,9 @@ extern "C" ipuc_status ipuc_gemm_f32(float *c, const float *a, const float *b, i
 //
 // The array is a device symbol, so on the host its name is only a stand-in:
 // its device address is resolved once per device with cudaGetSymbolAddress
-// (during the first call on that device, with that device current) and cached.
+// (during the first call on that device, with that device current) and cached
+// together with the current context, so that a call after cudaDeviceReset or
+// under another context resolves it again.
 // Every GPU that loads libipuc.so holds the array until the process exits.
 // All calls share it: two calls that overlap on the GPU (different streams, or
 // the same call issued concurrently from two host threads) race on it.  The
@@ -1027,20 +1153,51 @@ constexpr uint64_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB
 static __device__ __align__(256) uint8_t g_gemm_f32_scratch[kNoAllocScratchBytes];
 
 std::mutex g_scratch_mu;
-void *g_scratch_ptr[64] = {};
+// Cached device address of the array per device, with the context it was
+// resolved in: a module reloaded into a new context (after cudaDeviceReset, or
+// under a caller's non-primary context) places the array elsewhere, so a
+// context change re-resolves it.
+struct ScratchSlot {
+  void *ctx = nullptr;
+  void *ptr = nullptr;
+};
+ScratchSlot g_scratch_slot[64];
+
+using CtxGetCurrentFn = int (*)(void **);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
 
 ipuc_status scratch_address(void **out) {
   int dev = 0;
   IPUC_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(IPUC_ERR_UNSUPPORTED, "gemm_f32_noalloc: device index above 63");
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return fail(IPUC_ERR_CUDA, "gemm_f32_noalloc: cuCtxGetCurrent is unavailable");
+  void *ctx = nullptr;
+  if (get(&ctx) != 0) return fail(IPUC_ERR_CUDA, "gemm_f32_noalloc: cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
+  ScratchSlot &slot = g_scratch_slot[dev];
+  if (!ctx || !slot.ptr || slot.ctx != ctx) {
+    // With no context current yet, this runtime call makes the primary one
+    // current; the context is read again afterwards.
     void *p = nullptr;
     const cudaError_t err = cudaGetSymbolAddress(&p, g_gemm_f32_scratch);
     if (err != cudaSuccess) return cuda_fail(err, "gemm_f32_noalloc: cudaGetSymbolAddress(scratch)");
-    g_scratch_ptr[dev] = p;
+    if (!ctx && (get(&ctx) != 0 || !ctx)) return fail(IPUC_ERR_CUDA, "gemm_f32_noalloc: no current context");
+    slot.ctx = ctx;
+    slot.ptr = p;
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return IPUC_OK;
 }
 

@@ -164,6 +164,7 @@ ipuc_status lower(const ipug_graph &g, ipug_session &s, bool allocate = true) {
     if (is_output[r] || consumers[r].size() != 1) continue;
     const int32_t c = consumers[r][0];
     const Op &co = g.ops[c];
+    if (fused_gemm[c] >= 0) continue;  // Add(Gemm, Gemm): the second GEMM keeps its own step and buffer
     if (co.kind == OpKind::Gelu) {
       fused_into_next[i] = true;
       fused_gemm[c] = (int32_t)i;

@@ -292,3 +292,58 @@ def evaluate(graph, inputs: dict, threads: int = 8) -> dict:
             raise ValueError(op.kind)
         vals[op.result] = quantize_f16(np.ascontiguousarray(r, dtype=np.float32))
     return vals
+
+
+# --------------------------------------------------------------------------
+# Sampled checks of full-size workloads: the evaluator restricted to a few
+# output rows, so that a GPU result at BASELINE size can be compared in seconds
+# --------------------------------------------------------------------------
+
+F16_MAX_REL, F16_REL_L2 = 2e-2, 5e-3   # BASELINE FP16 tolerance
+
+
+def compare_f16(actual, ref, max_rel=F16_MAX_REL, rel_l2=F16_REL_L2) -> dict:
+    """max|err| / max|ref| and rel-L2 of `actual` against `ref`, with pass/fail
+    against the FP16 tolerance (max|err| <= 2e-2 max|ref|, rel-L2 <= 5e-3)."""
+    a = np.asarray(actual, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    err = np.abs(a - r)
+    mr = float(err.max() / max(np.abs(r).max(), 1e-30)) if err.size else 0.0
+    l2 = float(np.linalg.norm(a - r) / max(np.linalg.norm(r), 1e-30)) if err.size else 0.0
+    finite = bool(np.isfinite(a).all())
+    return {"max_err_over_max_ref": mr, "rel_l2": l2, "elements": int(err.size),
+            "pass": bool(finite and mr <= max_rel and l2 <= rel_l2)}
+
+
+def mlp_rows(x_rows, w) -> np.ndarray:
+    """Rows of the MLP up-projection graph GELU(X W) (config 3, GELU fused or
+    not): evaluate() quantises the GEMM result and the GELU result to f16."""
+    return quantize_f16(gelu(quantize_f16(gemm(quantize_f16(x_rows), quantize_f16(w)))))
+
+
+def block_rows(x_b, w: dict, heads: int, rows, threads: int = 8) -> np.ndarray:
+    """evaluate() of the transformer-block graph
+        h = Wo-proj(merge_heads(attention(split_heads(x Wq), split_heads(x Wk), split_heads(x Wv)))) + x
+        y = GELU(h W1) W2 + h
+    restricted to token rows `rows` of one batch element x_b [S, d].  A row's
+    attention reads K and V of every row of its batch element, so those two
+    projections are evaluated in full; everything else only for `rows`.
+    Every op result is quantised to f16 (diagnostic.rs:454-460)."""
+    q16 = quantize_f16
+    x_b = q16(x_b)
+    W = {n: q16(a) for n, a in w.items()}
+    rows = np.asarray(rows)
+    S, d = x_b.shape
+    dh = d // heads
+    xr = x_b[rows]
+    q = q16(gemm(xr, W["wq"]))
+    k = q16(gemm(x_b, W["wk"]))
+    v = q16(gemm(x_b, W["wv"]))
+    qh = np.ascontiguousarray(q.reshape(len(rows), heads, dh).transpose(1, 0, 2))
+    kh = np.ascontiguousarray(k.reshape(S, heads, dh).transpose(1, 0, 2))
+    vh = np.ascontiguousarray(v.reshape(S, heads, dh).transpose(1, 0, 2))
+    a = q16(attention(qh, kh, vh, threads=threads))
+    a = np.ascontiguousarray(a.transpose(1, 0, 2).reshape(len(rows), d))
+    h = q16(q16(gemm(a, W["wo"])) + xr)
+    u = q16(gelu(q16(gemm(h, W["w1"]))))
+    return q16(q16(gemm(u, W["w2"])) + h)

@@ -80,7 +80,8 @@ def test_gemm_f32_workspace_covers_both_splits():
     for m, n, k in [(1, 4, 4), (300, 260, 100), (4096, 4096, 4096), (2200, 4104, 1000)]:
         kp = (k + 7) // 8 * 8
         r = lambda x: (x + 255) // 256 * 256
-        f16 = 2 * r(m * kp * 2) + 2 * r(n * kp * 2) + r(m * 4) + 2 * r(n * 4)
+        # planes, exponents/maxima/tiny counts/fix-up flags, fix-up bitmap
+        f16 = 2 * r(m * kp * 2) + 2 * r(n * kp * 2) + 3 * r(m * 4) + 3 * r(n * 4) + r(m * ((n + 31) // 32) * 4)
         tf32 = 2 * r(m * k * 4) + 2 * r(k * n * 4)
         assert ipuc.gemm_f32_workspace_bytes(m, n, k) == max(f16, tf32)
 

@@ -139,3 +139,94 @@ def test_gemm_f32_split_k_tail(bt, split):
     assert rel_l2(got, ref) <= 1e-5
     again, _, _, _ = run(2200, 4104, 1000, (ipuc.GEMM_B_TRANSPOSED if bt else 0) | split, seed=37)
     assert np.array_equal(got, again)   # two atomic adds onto zero do not depend on their order
+
+
+def _elementwise_ok(got, a, b, bt, c0=None, rtol=1e-5, atol_rel=1e-6):
+    """|err_ij| <= rtol |ref_ij| + atol_rel (|A| |B|)_ij against fp64."""
+    a64, b64 = a.astype(np.float64), (b.T if bt else b).astype(np.float64)
+    ref = a64 @ b64 + (0 if c0 is None else c0)
+    scale = np.abs(a64) @ np.abs(b64) + (0 if c0 is None else np.abs(c0))
+    err = np.abs(got.astype(np.float64) - ref)
+    bad = err > rtol * np.abs(ref) + atol_rel * scale
+    return not bad.any(), f"{bad.sum()} elements off; worst {np.max(err / np.maximum(np.abs(ref), 1e-300)):.3g} rel"
+
+
+def _wide_rows(m, k, seed):
+    """Rows mixing 1.0 (in columns `big`) with values near 1e-8."""
+    rng = np.random.default_rng(seed)
+    a = (rng.uniform(-1, 1, (m, k)) * 1e-8).astype(np.float32)
+    big = rng.choice(k, max(1, k // 16), replace=False)
+    a[:, big] = 1.0
+    return a, big
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 384, 512), (2304, 2048, 1024)])
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_f32_wide_dynamic_range_rows(m, n, k, bt):
+    """Each row of A holds 1.0 and values near 1e-8; B is zero where A is 1.0,
+    so every C element is made of the tiny values alone.  The scaled split
+    alone loses ~10 bits here; the fix-up must give an fp32 result."""
+    a, big = _wide_rows(m, k, seed=m + k)
+    b = seeded_uniform(7, (k, n))
+    b[big, :] = 0.0
+    bb = np.ascontiguousarray(b.T) if bt else b
+    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    ws = torch.empty(ipuc.gemm_f32_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    ipuc.gemm_f32(c, dev_f32(a), dev_f32(bb), m, n, k, ws, ipuc.GEMM_B_TRANSPOSED if bt else 0)
+    got = host_f32(c)
+    ok, msg = _elementwise_ok(got, a, bb, bt)
+    assert ok, msg
+    ref = a.astype(np.float64) @ b.astype(np.float64)
+    assert rel_l2(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_f32_wide_dynamic_range_columns(bt):
+    """The same with the wide range along B's columns, A zero where B is big,
+    and IPUC_GEMM_ACCUMULATE onto a random C."""
+    m, n, k = 640, 520, 768
+    bcols, big = _wide_rows(n, k, seed=3)          # [n, k]: column j of B is row j here
+    b = np.ascontiguousarray(bcols.T)              # [k, n]
+    a = seeded_uniform(8, (m, k))
+    a[:, big] = 0.0
+    c0 = seeded_uniform(9, (m, n))
+    bb = bcols if bt else b
+    c = dev_f32(c0)
+    ws = torch.empty(ipuc.gemm_f32_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    ipuc.gemm_f32(c, dev_f32(a), dev_f32(bb), m, n, k, ws,
+                  ipuc.GEMM_ACCUMULATE | (ipuc.GEMM_B_TRANSPOSED if bt else 0))
+    ok, msg = _elementwise_ok(host_f32(c), a, bb, bt, c0=c0.astype(np.float64))
+    assert ok, msg
+
+
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_f32_non_finite_inputs(bt):
+    """inf, -inf and NaN inputs give the IEEE pattern of the evaluator's SGEMM
+    (oracle.gemm) element by element; everything else keeps the tolerance."""
+    m, n, k = 2304, 2048, 520       # a CTA-pair shape with a K tail
+    a = seeded_uniform(21, (m, k))
+    b = seeded_uniform(22, (k, n))
+    a[5, 7] = np.inf
+    a[300, 11] = -np.inf
+    a[301, 11] = np.inf
+    a[301, 12] = -np.inf            # +inf and -inf in one row: NaN wherever both meet finite nonzero B
+    a[1000, 100] = np.nan
+    b[11, 40] = 0.0                 # inf * 0 in column 40 for rows 300 and 301
+    b[200, 77] = np.inf
+    b[201, 1500] = np.nan
+    bb = np.ascontiguousarray(b.T) if bt else b
+    c = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    ws = torch.empty(ipuc.gemm_f32_workspace_bytes(m, n, k), dtype=torch.uint8, device="cuda")
+    ipuc.gemm_f32(c, dev_f32(a), dev_f32(bb), m, n, k, ws, ipuc.GEMM_B_TRANSPOSED if bt else 0)
+    got = host_f32(c)
+    with np.errstate(invalid="ignore", over="ignore"):
+        ref = oracle.gemm(a, b)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isposinf(got), np.isposinf(ref))
+    assert np.array_equal(np.isneginf(got), np.isneginf(ref))
+    fin = np.isfinite(ref)
+    assert fin.sum() > 0.99 * m * n
+    # elements outside the rows and columns that hold a non-finite input
+    r64 = np.where(np.isfinite(a), a, 0).astype(np.float64) @ np.where(np.isfinite(b), b, 0).astype(np.float64)
+    keep = fin & np.isfinite(a).all(1)[:, None] & np.isfinite(b).all(0)[None, :]
+    assert rel_l2(got[keep], r64[keep]) <= 1e-5

@@ -132,3 +132,20 @@ def test_unsupported_features_fail_loudly():
     with pytest.raises(ipuc.IpucError) as e:
         Session(g)
     assert e.value.status == ipuc.ERR_UNSUPPORTED
+
+
+def test_add_of_two_gemms():
+    """Add(Gemm(x, W1), Gemm(y, W2)): one GEMM fused with the Add, the other kept."""
+    g = ComputeGraph()
+    x = g.host_input("x", [192, 128])
+    y = g.host_input("y", [192, 96])
+    w1 = g.parameter("w1", [128, 256])
+    w2 = g.parameter("w2", [96, 256])
+    s = g.add(g.gemm(x, w1), g.gemm(y, w2))
+    g.set_outputs([s])
+    inputs = {x: seeded_normal(11, (192, 128)), y: seeded_normal(12, (192, 96)),
+              w1: seeded_normal(13, (128, 256), 0.1), w2: seeded_normal(14, (96, 256), 0.1)}
+    sess = run_graph(g, inputs)
+    assert sess.plan.count("gemm_f16+add") == 1
+    ok, msg = f16_close(sess.read(s).astype(np.float32), oracle.evaluate(g, inputs)[s])
+    assert ok, msg

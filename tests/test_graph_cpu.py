@@ -103,3 +103,14 @@ def test_plan_reports_unsupported_features():
     g.set_outputs([g.flash_attention_with_options(q, q, q, causal=True)])
     with pytest.raises(Exception, match="causal"):
         g.plan()
+
+
+def test_add_of_two_gemms_fuses_one():
+    """x W1 + y W2 with both products used once: the first GEMM's epilogue adds
+    the second GEMM's result, which keeps its own step and buffer."""
+    g = ComputeGraph()
+    x = g.host_input("x", [64, 128])
+    y = g.host_input("y", [64, 96])
+    s = g.add(g.gemm(x, g.parameter("w1", [128, 256])), g.gemm(y, g.parameter("w2", [96, 256])))
+    g.set_outputs([s])
+    assert labels(g.plan()) == ["gemm_f16", "gemm_f16+add"]

@@ -210,3 +210,62 @@ def test_staged_softmax_merge_equals_attention():
     out = acc[:, :D]
     err = np.abs(out - ref)
     assert err.max() <= 0.012 and np.sqrt((err ** 2).mean()) <= 0.003
+
+
+# ---- explicit index values of the storage orders (f16), computed by hand from
+# the closed forms of crates/ipu-codegen/src/storage.rs, so that a wrong but
+# bijective map in the oracle (and so in the bit-exact GPU tests) is caught.
+
+# AMP-Left (storage.rs:315-325): (c / 16) * rows * 16 + r * 16 + c % 16.
+# rows 4, cols 32.
+AMP_LEFT_KAT = [((0, 0), 0), ((0, 15), 15), ((1, 0), 16), ((3, 15), 63), ((0, 16), 64), ((2, 20), 100),
+                ((3, 31), 127)]
+# AMP-Output (storage.rs:329-340): pair p = (c % 16) / 2 lands at pair
+# (p % 4) * 2 + p / 4, i.e. logical columns 0..15 sit at physical columns
+# 0 1 4 5 8 9 12 13 2 3 6 7 10 11 14 15.  rows 2, cols 32.
+AMP_OUTPUT_COLUMN = [0, 1, 4, 5, 8, 9, 12, 13, 2, 3, 6, 7, 10, 11, 14, 15]
+AMP_OUTPUT_KAT = [((0, 2), 4), ((0, 8), 2), ((1, 8), 18), ((1, 13), 27), ((0, 16), 32), ((1, 27), 55),
+                  ((1, 31), 63)]
+# AMP-TransposedRight (storage.rs:326, 344-371, right_matrix_index on the
+# transposed extents): panel (r / 16) * (cols / 16) + c / 16, then
+# (r % 16) * 16 + c % 16 inside the 256-element panel.  rows 32, cols 32.
+AMP_TRANSPOSED_RIGHT_KAT = [((0, 0), 0), ((0, 1), 1), ((1, 0), 16), ((5, 20), 340), ((20, 3), 579),
+                            ((31, 31), 1023)]
+# BlockMajor{64, 16} (storage.rs:372-426): panel
+# (r / 64) * (cols / 16) * 4 + (c / 16) * 4 + (r % 64) / 16, then
+# (c % 16) * 16 + r % 16 inside the 256-element micro-block.  rows 128, cols 32.
+BLOCK_MAJOR_KAT = [((0, 0), 0), ((1, 0), 1), ((0, 1), 16), ((16, 0), 256), ((0, 16), 1024), ((70, 17), 3094),
+                   ((127, 31), 4095)]
+# BlockMajor transposed {64, 16}: the same map on the transposed matrix
+# (rows 32, cols 128: element (r, c) takes the index of (c, r) above).
+BLOCK_MAJOR_T_KAT = [((17, 70), 3094), ((31, 127), 4095), ((1, 0), 16), ((0, 1), 1)]
+
+
+@pytest.mark.parametrize("order,rows,cols,table", [
+    (oracle.AMP_LEFT, 4, 32, AMP_LEFT_KAT),
+    (oracle.AMP_OUTPUT, 2, 32, AMP_OUTPUT_KAT),
+    (oracle.AMP_TRANSPOSED_RIGHT, 32, 32, AMP_TRANSPOSED_RIGHT_KAT),
+    (oracle.BLOCK_MAJOR, 128, 32, BLOCK_MAJOR_KAT),
+    (oracle.BLOCK_MAJOR_TRANSPOSED, 32, 128, BLOCK_MAJOR_T_KAT),
+])
+def test_layout_index_known_values(order, rows, cols, table):
+    for (r, c), want in table:
+        assert oracle.layout_index(order, rows, cols, r, c) == want, (r, c)
+
+
+def test_amp_output_pair_swizzle_row():
+    """Every column of one 16-column micro-panel (storage.rs:333-336)."""
+    got = [oracle.layout_index(oracle.AMP_OUTPUT, 1, 16, 0, c) for c in range(16)]
+    assert got == AMP_OUTPUT_COLUMN
+
+
+@pytest.mark.parametrize("rows,cols,cb", [(256, 96, 16), (128, 256, 64), (512, 64, 32)])
+def test_block_major_span_offsets(rows, cols, cb):
+    """The span offset assertion of the block-major view test
+    (storage.rs:1034-1045): a view starting at row `inner` (a multiple of 64)
+    and column `column` (a multiple of the column block) starts at byte
+    ((inner / 64) * column_blocks + column / column_block) * 64 * column_block * 2."""
+    for inner in range(0, rows, 64):
+        for column in range(0, cols, cb):
+            want = ((inner // 64) * (cols // cb) + column // cb) * 64 * cb * 2
+            assert oracle.layout_index(oracle.BLOCK_MAJOR, rows, cols, inner, column, 64, cb) * 2 == want
