@@ -9,7 +9,9 @@
  * low.rs:1673-1709) replaced by a per-GPU lowering onto ipuc_* kernels:
  *   Gemm (+ a single-consumer Gelu)      -> ipuc_gemm_f16 with EPILOGUE_GELU
  *   Gemm (+ a single-consumer Add of a same-shaped value)
- *                                        -> copy of the addend + ipuc_gemm_f16 ACCUMULATE
+ *                                        -> ipuc_gemm_f16_addend (the epilogue adds the
+ *                                           other operand; batched GEMMs copy it and
+ *                                           accumulate)
  *   Gelu                                 -> ipuc_gelu_f16
  *   Add (same shape, or a trailing-suffix broadcast) -> ipuc_add_f16
  *   SplitHeads / MergeHeads              -> ipuc_split_heads_f16 / ipuc_merge_heads_f16
