@@ -718,9 +718,10 @@ def gather_outputs(torch, world, y, o):
 
 
 def transformer_block_tp(torch, rank, world):
-    """Config 5 over all ranks, Megatron tensor parallel (ipuc.tp): QKV and MLP-up
-    split by columns, output and MLP-down projections by rows, one NCCL
-    all-reduce after each half.  Device time, max over ranks; TFLOP/s of the
+    """Config 5 over all ranks through the sharded graph session (ipuc.tp):
+    the session derives the Megatron split from the block's graph (QKV and
+    MLP-up by columns, output and MLP-down projections by rows, one NCCL
+    all-reduce after each half).  Device time, max over ranks; TFLOP/s of the
     whole block."""
     from ipuc.tp import TensorParallelBlock
     B, S, d, H, ff = 4, 2048, 4096, 32, 16384
@@ -736,27 +737,23 @@ def transformer_block_tp(torch, rank, world):
     x = torch.randn((B * S, d), generator=g, device="cuda").half()
     stream = torch.cuda.current_stream()
 
-    def timed(chunks):
+    def timed():
         for _ in range(3):
-            blk.forward(x, chunks)
+            blk.forward(x)
         torch.cuda.synchronize()
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(5):
-            blk.forward(x, chunks)
+            blk.forward(x)
         e1.record(stream)
         torch.cuda.synchronize()
         return max_over_ranks(e0.elapsed_time(e1) / 5, world)
 
-    # whole-matrix all-reduces after each half, and the row-chunked pipeline
-    # (each chunk's all-reduce overlapping the next chunk's GEMMs)
-    per = {c: timed(c) for c in (1, 2, 4)}
-    best = min(per, key=per.get)
-    ms = per[best]
+    ms = timed()
     # parity (rank 0; the output is complete on every rank): 4 token rows of
     # the first and last batch element against the oracle's evaluation of the
-    # unsharded block, after an unchunked and a chunked forward
+    # unsharded block
     par = None
     if rank == 0:
         import numpy as np
@@ -767,23 +764,16 @@ def transformer_block_tp(torch, rank, world):
         sel = [(b, np.sort(pick.choice(S, 4, replace=False))) for b in (0, B - 1)]
         xh = x.float().cpu().numpy().reshape(B, S, d)
         refs = np.concatenate([oracle.block_rows(xh[b], host_w, H, r, threads=os.cpu_count() or 8) for b, r in sel])
-    outs = {}
-    for c in (1, best if best != 1 else 2):
-        yv = blk.forward(x, c)
-        torch.cuda.synchronize()
-        if rank == 0:
-            yh = yv.float().cpu().numpy().reshape(B, S, d)
-            outs[c] = np.concatenate([yh[b, r] for b, r in sel])
+    yv = blk.forward(x)
+    torch.cuda.synchronize()
     if rank == 0:
-        res = [oracle.compare_f16(v, refs) for v in outs.values()]
-        par = {"max_err_over_max_ref": max(r["max_err_over_max_ref"] for r in res),
-               "rel_l2": max(r["rel_l2"] for r in res), "pass": all(r["pass"] for r in res),
-               "token_rows": 8, "chunks_checked": sorted(outs), "seconds": round(time.perf_counter() - t0, 1)}
+        yh = yv.float().cpu().numpy().reshape(B, S, d)
+        par = oracle.compare_f16(np.concatenate([yh[b, r] for b, r in sel]), refs)
+        par.update(token_rows=8, seconds=round(time.perf_counter() - t0, 1))
     barrier(world)
     return {"parity": par, "ms": round(ms, 4), "tflops": round(blk.flop / (ms * 1e-3) / 1e12, 1), "flop": blk.flop,
-            "parallelism": f"tp{world}", "chunks": best,
-            "ms_by_chunks": {str(c): round(v, 4) for c, v in per.items()},
-            "collective": "2 NCCL all-reduces of 64 MiB (f16) per block, in `chunks` row blocks"}
+            "parallelism": f"tp{world}", "steps": blk.session.plan.count("\n") - 1,
+            "collective": "2 NCCL all-reduces of 64 MiB (f16) per block, derived from the graph by the sharded session"}
 
 
 # ---------------------------------------------------------------------------

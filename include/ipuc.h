@@ -101,7 +101,11 @@ enum {
   /* ipuc_gemm_f32 only: the classic three-pass TF32 split (hi = tf32(x),
    * lo = tf32(x - hi), kind::tf32 MMAs) instead of the default scaled f16
    * split; same accuracy class, about 0.6x the throughput. */
-  IPUC_GEMM_F32_SPLIT_TF32 = 1u << 4
+  IPUC_GEMM_F32_SPLIT_TF32 = 1u << 4,
+  /* ipuc_gemm_f16: A stored transposed, as [k x m] (lda >= m, m a multiple
+   * of 8): GemmOptions::transpose_left (graph.rs:126-129).  The tensor cores
+   * read it M-major straight from memory (no transpose copy). */
+  IPUC_GEMM_A_TRANSPOSED = 1u << 5
 };
 ipuc_status ipuc_gemm_f16(void *c, const void *a, const void *b, int64_t m, int64_t n, int64_t k,
                           int64_t lda, int64_t ldb, int64_t ldc, uint32_t flags,

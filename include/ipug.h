@@ -18,8 +18,10 @@
  *   FlashAttention (non-causal)          -> ipuc_flash_attention_f16
  * Every value is stored as f16 in its own device buffer (the evaluator's
  * per-op-result quantisation, crates/ipu-tests/src/diagnostic.rs:454-460).
- * Unsupported graph features (transpose_left, causal attention — rejected by
- * the reference too, operator.rs:997 — general broadcasting, Repeat) make
+ *   Gemm with transpose_left               -> IPUC_GEMM_A_TRANSPOSED (M-major A)
+ *   Repeat                               -> unrolled, one body copy per iteration
+ * Unsupported graph features (causal attention — rejected by the reference
+ * too, operator.rs:997 — and broadcasting other than a trailing suffix) make
  * ipug_session_open fail with IPUC_ERR_UNSUPPORTED.
  */
 #ifndef IPUG_H
@@ -62,16 +64,87 @@ int32_t ipug_value_shape(const ipug_graph *g, int32_t value, uint32_t *dims);
  * lowering errors (IPUC_ERR_UNSUPPORTED) as ipug_session_open reports them. */
 ipuc_status ipug_graph_plan(const ipug_graph *g, char *buf, uint64_t size, uint64_t *needed);
 
-/* Session: lower the graph for `device`, allocate every value's buffer. */
+/* ---- Repeat regions (graph.rs:294-313, 382-473) ----
+ * A value sequence names same-shaped values (e.g. per-layer weights); a Repeat
+ * runs its body `count` times with carried values (threaded from one
+ * iteration's yields to the next iteration's arguments), invariants, and one
+ * entry of each iterated sequence per iteration.  ipug_repeat_begin writes
+ * the body's argument value ids (carried, then invariants, then iterated) to
+ * `arguments`; operations added until ipug_repeat_end form the body and may
+ * use only those arguments and the body's own results.  ipug_repeat_end takes
+ * one yield per carried value (same shape) and writes the Repeat's result ids
+ * to `results`; it returns the number of results, or -1 (the body is then
+ * discarded).  Errors follow GraphError's texts. */
+int32_t ipug_value_sequence(ipug_graph *g, const char *name, const int32_t *values, int32_t count);
+ipuc_status ipug_repeat_begin(ipug_graph *g, uint32_t count, const int32_t *carried, int32_t carried_count,
+                              const int32_t *invariants, int32_t invariant_count, const int32_t *sequences,
+                              int32_t sequence_count, int32_t *arguments);
+int32_t ipug_repeat_end(ipug_graph *g, const int32_t *yields, int32_t yield_count, int32_t *results);
+
+/* ---- Sessions ----
+ * A session lowers the graph for one GPU and allocates every value's buffer.
+ * With world > 1 it is one rank of a sharded session over `world` GPUs (one
+ * process or thread per GPU, each opening its own rank with the same graph
+ * and the same NCCL unique id): every rank derives its shard of the work from
+ * the graph (column-split GEMMs -> head-local attention -> row-split GEMMs,
+ * with an NCCL all-reduce where a row split's partial sums meet a consumer
+ * that needs the whole value, an all-gather where a column split does), and
+ * the session owns the NCCL communicator.  fuse = 0 keeps a buffer for every
+ * operation result (no epilogue or attention fusion), for per-op diagnostics. */
+typedef struct ipug_session_options {
+  int32_t device;
+  int32_t rank, world;   /* world 1: a single-GPU session */
+  const void *nccl_id;   /* world > 1: 128-byte ncclUniqueId from ipug_nccl_unique_id on one rank */
+  int32_t fuse;          /* 1: fused lowering (default); 0: every value kept */
+} ipug_session_options;
+
+ipug_session *ipug_session_open_ex(const ipug_graph *g, const ipug_session_options *options, ipuc_status *status);
+/* A new NCCL unique id (ncclGetUniqueId) into out[0..128). */
+ipuc_status ipug_nccl_unique_id(void *out, uint64_t size);
+/* The plan ipug_session_open_ex would run with `options`, without a device
+ * (as ipug_graph_plan; a sharded plan starts with "# rank r of w"). */
+ipuc_status ipug_graph_plan_ex(const ipug_graph *g, const ipug_session_options *options, char *buf, uint64_t size,
+                               uint64_t *needed);
+/* Rank `rank`'s shard of the graph as JSON, without a device: values (local
+ * shape, state replicated/columns/heads/partial, parameter slice), operations
+ * (including the inserted all_reduce / all_gather_columns) and outputs. */
+ipuc_status ipug_graph_shard_json(const ipug_graph *g, int32_t rank, int32_t world, char *buf, uint64_t size,
+                                  uint64_t *needed);
+
+/* Session: lower the graph for `device`, allocate every value's buffer
+ * (ipug_session_open_ex with world 1 and fuse 1). */
 ipug_session *ipug_session_open(const ipug_graph *g, int32_t device, ipuc_status *status);
 void ipug_session_close(ipug_session *s);
-/* Copy f16 host data into an input/parameter (or any) value; bytes must equal
- * the value's element count * 2.  Stream-ordered on `stream`. */
+/* Copy f16 data (host or device memory) into an input/parameter (or any)
+ * value; bytes must equal the value's element count * 2.  In a sharded
+ * session a parameter the rank holds a slice of takes the whole parameter
+ * (the rank copies its columns or rows) or exactly its slice's bytes.
+ * Stream-ordered on `stream`.  Values inside a Repeat body are not
+ * addressable (the Repeat's results are). */
 ipuc_status ipug_session_write(ipug_session *s, int32_t value, const void *host, uint64_t bytes, ipuc_stream stream);
 ipuc_status ipug_session_read(ipug_session *s, int32_t value, void *host, uint64_t bytes, ipuc_stream stream);
 /* Device pointer of a value's buffer (for callers that keep data on the GPU). */
 void *ipug_session_device_ptr(ipug_session *s, int32_t value);
 ipuc_status ipug_session_run(ipug_session *s, ipuc_stream stream);
+
+/* ---- Per-op diagnostic (build_diagnostic_package, crates/ipu-codegen/src/
+ * package.rs:543; service_checkpoint, crates/ipu-tests/src/diagnostic.rs:
+ * 92-199) ----
+ * After a run, compare each listed value's buffer with caller-supplied f32
+ * reference values (e.g. the host evaluator's): one report per value.  A
+ * value fused into its consumer (open the session with fuse = 0 to keep
+ * every value), inside a Repeat body, or held as a shard on this rank is
+ * reported with available = 0. */
+typedef struct ipug_value_report {
+  int32_t value;
+  int32_t producer;      /* graph operation id of the step that wrote it (-1: an input) */
+  int32_t available;
+  uint64_t elements;
+  uint64_t nonfinite;    /* non-finite device elements (left out of the errors) */
+  double max_abs_err, max_abs_ref, rel_l2;
+} ipug_value_report;
+ipuc_status ipug_session_diagnose(ipug_session *s, const int32_t *values, const float *const *reference,
+                                  int32_t count, ipug_value_report *reports, ipuc_stream stream);
 /* Run once with a CUDA event pair around every lowered step and write a JSON
  * report (one record per step: op ids, kernel, ms, FLOP or bytes) into buf —
  * the event-timed counterpart of the reference's cycle ProfileReport

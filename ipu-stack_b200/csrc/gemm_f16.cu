@@ -130,7 +130,7 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int b, int64_t 
   }
 }
 
-template <bool kBKMajor>
+template <bool kAKMajor, bool kBKMajor>
 __global__ void __launch_bounds__(192, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmParams p) {
@@ -184,7 +184,12 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t *a_s = smem + s * STAGE_BYTES;
           uint8_t *b_s = a_s + A_BYTES;
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tma_load_3d(a_s, &tmA, &full[s], kb * BK, mt * BM, b);
+          if (kAKMajor) {
+            tma_load_3d(a_s, &tmA, &full[s], kb * BK, mt * BM, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_3d(a_s + j * 8192, &tmA, &full[s], mt * BM + j * 64, kb * BK, b);
+          }
           if (kBKMajor) {
             tma_load_3d(b_s, &tmB, &full[s], kb * BK, nt * BN, b);
           } else {
@@ -200,10 +205,10 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(BM, BN, /*f16*/ 0, false, !kBKMajor);
+      constexpr uint32_t idesc = make_idesc(BM, BN, /*f16*/ 0, !kAKMajor, !kBKMajor);
       uint32_t it = 0, local = 0;
       bool ok = true;
-      const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), kAKMajor ? 16 : 8192, 1024, kSwizzle128B);
       const uint64_t b_desc0 = make_smem_desc(smem_u32(smem) + A_BYTES, kBKMajor ? 16 : 8192, 1024, kSwizzle128B);
       for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
         const uint32_t buf = local & 1u, use = local >> 1;
@@ -227,7 +232,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t bd = b_desc0 + (uint64_t)(s * (STAGE_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = ad + (uint64_t)((k * 32) >> 4);
+            const uint64_t adesc = ad + (uint64_t)((kAKMajor ? k * 32 : k * 2048) >> 4);
             const uint64_t bdesc = bd + (uint64_t)((kBKMajor ? k * 32 : k * 2048) >> 4);
             mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
@@ -299,7 +304,7 @@ constexpr int P_STAGES = 6;
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr int PAIR_BM = 2 * BM;                // 256 rows per pair tile
 
-template <bool kBKMajor>
+template <bool kAKMajor, bool kBKMajor>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_f16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const GemmParams p) {
@@ -356,7 +361,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           uint8_t *a_s = smem + s * P_STAGE_BYTES;
           uint8_t *b_s = a_s + P_A_BYTES;
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * P_STAGE_BYTES);
-          tma_load_3d_pair(a_s, &tmA, &full[s], kb * BK, mt * PAIR_BM + (int)rank * BM, b);
+          if (kAKMajor) {
+            tma_load_3d_pair(a_s, &tmA, &full[s], kb * BK, mt * PAIR_BM + (int)rank * BM, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_3d_pair(a_s + j * 8192, &tmA, &full[s], mt * PAIR_BM + (int)rank * BM + j * 64, kb * BK, b);
+          }
           if (kBKMajor) {
             tma_load_3d_pair(b_s, &tmB, &full[s], kb * BK, nt * BN + (int)rank * PB_N, b);
           } else {
@@ -373,10 +384,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*f16*/ 0, false, !kBKMajor);
+      constexpr uint32_t idesc = make_idesc(PAIR_BM, BN, /*f16*/ 0, !kAKMajor, !kBKMajor);
       uint32_t it = 0, local = 0;
       bool ok = true;
-      const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), kAKMajor ? 16 : 8192, 1024, kSwizzle128B);
       const uint64_t b_desc0 = make_smem_desc(smem_u32(smem) + P_A_BYTES, kBKMajor ? 16 : 8192, 1024, kSwizzle128B);
       for (int64_t t = pair; t < p.num_tiles && ok; t += pairs, ++local) {
         const uint32_t buf = local & 1u, use = local >> 1;
@@ -400,7 +411,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           const uint64_t bd = b_desc0 + (uint64_t)(s * (P_STAGE_BYTES >> 4));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = ad + (uint64_t)((k * 32) >> 4);
+            const uint64_t adesc = ad + (uint64_t)((kAKMajor ? k * 32 : k * 2048) >> 4);
             const uint64_t bdesc = bd + (uint64_t)((kBKMajor ? k * 32 : k * 2048) >> 4);
             mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
@@ -459,19 +470,28 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
                             int64_t lda, int64_t ldb, int64_t ldc, int64_t sa, int64_t sb, int64_t sc,
                             uint32_t flags, cudaStream_t stream, const void *addend = nullptr, int64_t ld_add = 0) {
   IPUC_CHECK_ARG(m >= 0 && n >= 0 && k >= 0 && batch >= 0, "gemm_f16: negative extent");
-  IPUC_CHECK_ARG((flags & ~0xfu) == 0, "gemm_f16: unknown flag");
+  IPUC_CHECK_ARG((flags & ~(uint32_t)(IPUC_GEMM_ACCUMULATE | IPUC_GEMM_B_TRANSPOSED | IPUC_GEMM_OUT_F32 |
+                                       IPUC_GEMM_EPILOGUE_GELU | IPUC_GEMM_A_TRANSPOSED)) == 0,
+                 "gemm_f16: unknown flag");
   if (m == 0 || n == 0 || batch == 0) return IPUC_OK;
   IPUC_CHECK_ARG(k > 0, "gemm_f16: k must be positive");
   IPUC_CHECK_ARG(a && b && c, "gemm_f16: null pointer");
-  const bool bt = (flags & IPUC_GEMM_B_TRANSPOSED) != 0;
-  IPUC_CHECK_ARG(lda >= k && ldc >= n && ldb >= (bt ? k : n), "gemm_f16: leading dimension too small");
+  const bool bt = (flags & IPUC_GEMM_B_TRANSPOSED) != 0, at = (flags & IPUC_GEMM_A_TRANSPOSED) != 0;
+  IPUC_CHECK_ARG(lda >= (at ? m : k) && ldc >= n && ldb >= (bt ? k : n), "gemm_f16: leading dimension too small");
   IPUC_CHECK_ALIGN(aligned(a, 16) && aligned(b, 16) && aligned(c, 16), "gemm_f16: pointers must be 16-byte aligned");
-  IPUC_CHECK_ALIGN(lda % 8 == 0 && ldb % 8 == 0 && k % 8 == 0,
-                   "gemm_f16: lda, ldb and k must be multiples of 8 elements (16-byte TMA rows)");
+  IPUC_CHECK_ALIGN(lda % 8 == 0 && ldb % 8 == 0 && k % 8 == 0 && (!at || m % 8 == 0),
+                   "gemm_f16: lda, ldb and k (m too with IPUC_GEMM_A_TRANSPOSED) must be multiples of 8 elements "
+                   "(16-byte TMA rows)");
   IPUC_CHECK_ALIGN(batch == 1 || (sa % 8 == 0 && sb % 8 == 0), "gemm_f16: batch strides must be multiples of 8");
   IPUC_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31) && batch < (1ll << 31), "gemm_f16: extent too large");
   CUtensorMap ta, tb;
-  ipuc_status st = make_map_3d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, batch, lda, batch > 1 ? sa : 0, BK, BM);
+  // A: K-major [m x k] tiles of 128 x 64, or with IPUC_GEMM_A_TRANSPOSED
+  // M-major ([k x m] rows, 64-row boxes of 64 k).
+  auto map_a = [&](CUtensorMap *map) {
+    return at ? make_map_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, m, k, batch, lda, batch > 1 ? sa : 0, 64, BK)
+              : make_map_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, batch, lda, batch > 1 ? sa : 0, BK, BM);
+  };
+  ipuc_status st = map_a(&ta);
   if (st != IPUC_OK) return st;
   if (bt) st = make_map_3d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, k, n, batch, ldb, batch > 1 ? sb : 0, BK, BN);
   else st = make_map_3d(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, n, k, batch, ldb, batch > 1 ? sb : 0, 64, BK);
@@ -496,31 +516,29 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
     p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
     const int64_t pairs = p.num_tiles < sms / 2 ? p.num_tiles : sms / 2;
     CUtensorMap tap, tbp;
-    st = make_map_3d(&tap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, k, m, batch, lda, batch > 1 ? sa : 0, BK, BM);
+    st = map_a(&tap);
     if (st != IPUC_OK) return st;
     if (bt) st = make_map_3d(&tbp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, k, n, batch, ldb, batch > 1 ? sb : 0, BK, PB_N);
     else st = make_map_3d(&tbp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, n, k, batch, ldb, batch > 1 ? sb : 0, 64, BK);
     if (st != IPUC_OK) return st;
-    if (bt) {
-      IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-      gemm_f16_pair_kernel<true><<<(unsigned)(2 * pairs), 192, P_SMEM_BYTES, stream>>>(tap, tbp, p);
-    } else {
-      IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-      gemm_f16_pair_kernel<false><<<(unsigned)(2 * pairs), 192, P_SMEM_BYTES, stream>>>(tap, tbp, p);
-    }
-    return check_launch("gemm_f16_pair_kernel");
+    auto go = [&](auto kernel) -> ipuc_status {
+      IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+      kernel<<<(unsigned)(2 * pairs), 192, P_SMEM_BYTES, stream>>>(tap, tbp, p);
+      return check_launch("gemm_f16_pair_kernel");
+    };
+    if (at) return bt ? go(gemm_f16_pair_kernel<false, true>) : go(gemm_f16_pair_kernel<false, false>);
+    return bt ? go(gemm_f16_pair_kernel<true, true>) : go(gemm_f16_pair_kernel<true, false>);
   }
   p.tiles_m = (int32_t)((m + BM - 1) / BM);
   p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
   const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
-  if (bt) {
-    IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    gemm_f16_kernel<true><<<grid, 192, SMEM_BYTES, stream>>>(ta, tb, p);
-  } else {
-    IPUC_CUDA(cudaFuncSetAttribute(gemm_f16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    gemm_f16_kernel<false><<<grid, 192, SMEM_BYTES, stream>>>(ta, tb, p);
-  }
-  return check_launch("gemm_f16_kernel");
+  auto go = [&](auto kernel) -> ipuc_status {
+    IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    kernel<<<grid, 192, SMEM_BYTES, stream>>>(ta, tb, p);
+    return check_launch("gemm_f16_kernel");
+  };
+  if (at) return bt ? go(gemm_f16_kernel<false, true>) : go(gemm_f16_kernel<false, false>);
+  return bt ? go(gemm_f16_kernel<true, true>) : go(gemm_f16_kernel<true, false>);
 }
 
 }  // namespace

@@ -28,6 +28,7 @@ F16, F32 = 0, 1
 # gemm flags
 GEMM_ACCUMULATE, GEMM_B_TRANSPOSED, GEMM_OUT_F32, GEMM_EPILOGUE_GELU = 1, 2, 4, 8
 GEMM_F32_SPLIT_TF32 = 16  # ipuc_gemm_f32: the unscaled 3xTF32 split instead of the scaled f16 one
+GEMM_A_TRANSPOSED = 32    # ipuc_gemm_f16: A stored [k x m] (GemmOptions::transpose_left)
 
 # Every exported entry point with its argument types (kept in sync with
 # include/ipuc.h; tests check the library exports each one).
@@ -146,7 +147,7 @@ def fill_zero(out, nbytes=None, stream=None):
 
 def gemm_f16(c, a, b, m, n, k, lda=None, ldb=None, ldc=None, flags=0, stream=None):
     bt = bool(flags & GEMM_B_TRANSPOSED)
-    lda = k if lda is None else lda
+    lda = (m if flags & GEMM_A_TRANSPOSED else k) if lda is None else lda
     ldb = (k if bt else n) if ldb is None else ldb
     ldc = n if ldc is None else ldc
     call("ipuc_gemm_f16", _ptr(c), _ptr(a), _ptr(b), m, n, k, lda, ldb, ldc, flags, _stream(stream))
@@ -166,7 +167,8 @@ def gemm_f16_addend(c, a, b, m, n, k, addend, ld_addend=None, lda=None, ldb=None
 def gemm_f16_batched(c, a, b, batch, m, n, k, flags=0, stream=None):
     bt = bool(flags & GEMM_B_TRANSPOSED)
     ldb = k if bt else n
-    call("ipuc_gemm_f16_batched", _ptr(c), _ptr(a), _ptr(b), batch, m, n, k, k, ldb, n, m * k, n * k, m * n, flags,
+    lda = m if flags & GEMM_A_TRANSPOSED else k
+    call("ipuc_gemm_f16_batched", _ptr(c), _ptr(a), _ptr(b), batch, m, n, k, lda, ldb, n, m * k, n * k, m * n, flags,
          _stream(stream))
 
 

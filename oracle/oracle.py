@@ -268,7 +268,39 @@ def evaluate(graph, inputs: dict, threads: int = 8) -> dict:
     result is quantised to f16 (diagnostic.rs:454-460).  Returns a dict of
     value id -> f32 array."""
     vals = {v: quantize_f16(np.asarray(a, dtype=np.float32)) for v, a in inputs.items()}
-    for op in graph.operations:
+    _evaluate_ops(graph.operations, vals, threads)
+    return vals
+
+
+def _repeat(op, vals, threads):
+    """repeat_values (diagnostic.rs:467-520): the body runs `count` times on a
+    copy of the values, carried arguments bound to the previous iteration's
+    yields, invariants to the Repeat's invariant operands and iterated
+    arguments to entry `iteration` of each sequence."""
+    o = op.options
+    nc, ni = o["carried"], o["invariants"]
+    carried = [vals[v] for v in op.inputs[:nc]]
+    invariants = [vals[v] for v in op.inputs[nc:nc + ni]]
+    args = o["arguments"]
+    for it in range(o["count"]):
+        local = dict(vals)
+        for a, x in zip(args[:nc], carried):
+            local[a] = x
+        for a, x in zip(args[nc:nc + ni], invariants):
+            local[a] = x
+        for a, seq in zip(args[nc + ni:], o["sequences"]):
+            local[a] = vals[seq[it]]
+        _evaluate_ops(o["body"], local, threads)
+        carried = [local[y] for y in o["yields"]]
+    for r, x in zip(o["results"], carried):
+        vals[r] = x
+
+
+def _evaluate_ops(operations, vals, threads):
+    for op in operations:
+        if op.kind == "repeat":
+            _repeat(op, vals, threads)
+            continue
         ins = [vals[i] for i in op.inputs]
         if op.kind == "gemm":
             r = gemm(ins[0], ins[1], op.options["transpose_left"], op.options["transpose_right"])
@@ -291,7 +323,6 @@ def evaluate(graph, inputs: dict, threads: int = 8) -> dict:
         else:
             raise ValueError(op.kind)
         vals[op.result] = quantize_f16(np.ascontiguousarray(r, dtype=np.float32))
-    return vals
 
 
 # --------------------------------------------------------------------------

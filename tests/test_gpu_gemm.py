@@ -151,3 +151,31 @@ def test_gemm_batched_random():
 
 def test_gemm_device_status_clean():
     ipuc.device_status()
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 256), (128, 192, 64), (1024, 2048, 512), (304, 200, 136),
+                                   (2048, 2048, 1024)])
+@pytest.mark.parametrize("bt", [False, True])
+def test_gemm_a_transposed(m, n, k, bt):
+    """GemmOptions::transpose_left: A stored [k x m], read M-major by the
+    tensor cores (single-CTA and CTA-pair kernels, with either B layout)."""
+    at = oracle.f16_bits(seeded_normal(m + 1, (k, m), 0.1))
+    b = oracle.f16_bits(seeded_normal(n + 2, (n, k) if bt else (k, n), 0.1))
+    ref = oracle.quantize_f16(oracle.gemm(f16_of(at), f16_of(b), True, bt))
+    c = empty_u16(m * n)
+    flags = ipuc.GEMM_A_TRANSPOSED | (ipuc.GEMM_B_TRANSPOSED if bt else 0)
+    ipuc.gemm_f16(c, dev_u16(at), dev_u16(b), m, n, k, flags=flags)
+    ok, msg = f16_close(f16_of(host_u16(c)).reshape(m, n), ref)
+    assert ok, msg
+
+
+def test_gemm_a_transposed_batched_gelu():
+    batch, m, n, k = 3, 384, 256, 192
+    at = oracle.f16_bits(seeded_normal(5, (batch, k, m), 0.1))
+    b = oracle.f16_bits(seeded_normal(6, (batch, k, n), 0.1))
+    ref = oracle.quantize_f16(oracle.gelu(oracle.quantize_f16(oracle.gemm(f16_of(at), f16_of(b), True, False))))
+    c = empty_u16(batch * m * n)
+    ipuc.gemm_f16_batched(c, dev_u16(at), dev_u16(b), batch, m, n, k,
+                          flags=ipuc.GEMM_A_TRANSPOSED | ipuc.GEMM_EPILOGUE_GELU)
+    ok, msg = f16_close(f16_of(host_u16(c)).reshape(batch, m, n), ref)
+    assert ok, msg

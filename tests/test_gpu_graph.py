@@ -149,3 +149,87 @@ def test_add_of_two_gemms():
     assert sess.plan.count("gemm_f16+add") == 1
     ok, msg = f16_close(sess.read(s).astype(np.float32), oracle.evaluate(g, inputs)[s])
     assert ok, msg
+
+
+def test_repeat_mlp_blocks():
+    """The SiglipMlpBenchmark graph (main.rs:707-756): GEMM-GELU-GEMM blocks in
+    a Repeat over sequences of [1, k, n] weights, unrolled by the lowering,
+    against repeat_values' evaluation (diagnostic.rs:467-520)."""
+    from test_graph_cpu import mlp_repeat
+    g, x, ups, downs, y = mlp_repeat(blocks=4, d=256, hidden=1024)
+    rng = np.random.default_rng(13)
+    inputs = {x: rng.standard_normal(g.value_shape(x)).astype(np.float32)}
+    for v in ups + downs:
+        inputs[v] = (rng.standard_normal(g.value_shape(v)) * 0.06).astype(np.float32)
+    s = run_graph(g, inputs)
+    assert s.plan.count("gemm_f16+gelu") == 4
+    ok, msg = f16_close(s.read(y).astype(np.float32), oracle.evaluate(g, inputs)[y])
+    assert ok, msg
+
+
+def test_repeat_carried_gemm_output_is_double_buffered():
+    """A body whose yield is a GEMM of the carried value: iteration i+1 reads
+    iteration i's yield while writing its own, so the two live in different
+    buffers; an invariant residual is added every iteration."""
+    g = ComputeGraph()
+    x = g.host_input("x", [256, 128])
+    r = g.host_input("r", [256, 128])
+    ws = [g.parameter(f"w{i}", [128, 128]) for i in range(5)]
+    sq = g.value_sequence("weights", ws)
+    y = g.repeat(5, [x], [r], [sq], lambda b, a: [b.add(b.gemm(a.carried[0], a.iterated[0]), a.invariants[0])])[0]
+    g.set_outputs([y])
+    inputs = {x: seeded_normal(21, (256, 128)), r: seeded_normal(22, (256, 128), 0.1)}
+    for i, w in enumerate(ws):
+        inputs[w] = seeded_normal(30 + i, (128, 128), 0.08)
+    s = run_graph(g, inputs)
+    assert s.plan.count("gemm_f16+add") == 5
+    ok, msg = f16_close(s.read(y).astype(np.float32), oracle.evaluate(g, inputs)[y])
+    assert ok, msg
+
+
+def test_transpose_left_gemm():
+    g = ComputeGraph()
+    a = g.host_input("a", [192, 256])      # [k, m]
+    b = g.parameter("b", [192, 320])
+    c = g.gelu(g.gemm_with_options(a, b, transpose_left=True))
+    g.set_outputs([c])
+    inputs = {a: seeded_normal(41, (192, 256)), b: seeded_normal(42, (192, 320), 0.1)}
+    s = run_graph(g, inputs)
+    assert "gemm_f16+gelu" in s.plan
+    ok, msg = f16_close(s.read(c).astype(np.float32), oracle.evaluate(g, inputs)[c])
+    assert ok, msg
+
+
+def test_per_op_diagnostic_walks_every_value():
+    """ipug_session_diagnose on the config-5 block structure at reduced size:
+    with fuse=False every operation's result keeps a buffer, and each one is
+    compared with the evaluator's value (service_checkpoint,
+    diagnostic.rs:92-199); with the fused lowering the fused-away values are
+    reported unavailable."""
+    B, S, d, H, ff = 2, 256, 256, 4, 1024
+    g, x, ws, out = build_block(B, S, d, H, ff)
+    rng = np.random.default_rng(7)
+    inputs = {x: rng.standard_normal((B, S, d)).astype(np.float32)}
+    for n, v in ws.items():
+        inputs[v] = (rng.standard_normal(g.value_shape(v)) * 0.02).astype(np.float32)
+    ref = oracle.evaluate(g, inputs)
+    op_values = [op.result for op in g.operations]
+    s = Session(g, fuse=False)
+    for v, a in inputs.items():
+        s.write(v, a)
+    s.run()
+    assert "flash_attention_f16" in s.plan and "split_heads_f16" in s.plan and "gelu_f16" in s.plan
+    reports = s.diagnose({v: ref[v] for v in op_values})
+    assert len(reports) == len(op_values) == 14
+    for r in reports:
+        assert r["available"] and r["nonfinite"] == 0, r
+        assert r["max_abs_err"] <= 2e-2 * r["max_abs_ref"] and r["rel_l2"] <= 5e-3, r
+    assert [r["producer"] for r in reports] == list(range(len(op_values)))
+    s.close()
+    fused = Session(g)
+    for v, a in inputs.items():
+        fused.write(v, a)
+    fused.run()
+    avail = {r["value"]: r["available"] for r in fused.diagnose({v: ref[v] for v in op_values})}
+    assert avail[out] and not all(avail.values())
+    fused.close()

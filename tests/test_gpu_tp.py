@@ -1,6 +1,7 @@
-"""Tensor-parallel transformer block (ipuc.tp) against the oracle's evaluation
-of the same ComputeGraph: one rank on one GPU, and two ranks over NCCL when
-the box has two GPUs."""
+"""Tensor-parallel transformer block (ipuc.tp, a client of the sharded graph
+session) against the oracle's evaluation of the same ComputeGraph: one rank on
+one GPU, and two ranks over NCCL when the box has two GPUs; plus a sharded
+session of a Repeat graph opened directly through ipug_session_open_ex."""
 import os
 import socket
 
@@ -29,11 +30,11 @@ def block_inputs():
     return inputs[x].reshape(B * S, d), weights, ref
 
 
-def run_rank(rank, world, x, weights, chunks=1):
+def run_rank(rank, world, x, weights):
     from ipuc.tp import TensorParallelBlock
     blk = TensorParallelBlock(B, S, d, H, ff, rank, world)
     blk.load({n: torch.from_numpy(a).half() for n, a in weights.items()})
-    y = blk.forward(torch.from_numpy(x).half().cuda(), chunks=chunks)
+    y = blk.forward(torch.from_numpy(x).half().cuda())
     torch.cuda.synchronize()
     return y.float().cpu().numpy()
 
@@ -53,10 +54,7 @@ def _nccl_worker(rank, world, port, q):
     try:
         x, weights, ref = block_inputs()
         got = run_rank(rank, world, x, weights)
-        # the row-chunked pipeline (all-reduce of each block overlapping the
-        # next block's GEMMs) computes the same sums
-        piped = run_rank(rank, world, x, weights, chunks=4)
-        q.put((rank,) + f16_close(got, ref) + f16_close(piped, ref))
+        q.put((rank,) + f16_close(got, ref))
     finally:
         dist.destroy_process_group()
 
@@ -77,6 +75,46 @@ def test_tp_block_two_ranks_nccl():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, ok, msg, ok_piped, msg_piped in res:
+    for rank, ok, msg in res:
         assert ok, f"rank {rank}: {msg}"
-        assert ok_piped, f"rank {rank}, chunks=4: {msg_piped}"
+
+
+def _repeat_worker(rank, world, nccl_id, q):
+    """One rank of a sharded session of the MLP-blocks Repeat graph, opened
+    with the NCCL unique id the parent made (no torch.distributed at all)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    from ipuc.graph import Session
+    from test_graph_cpu import mlp_repeat
+    g, x, ups, downs, y = mlp_repeat(blocks=3, d=256, hidden=1024)
+    rng = np.random.default_rng(3)
+    inputs = {x: rng.standard_normal(g.value_shape(x)).astype(np.float32)}
+    for v in ups + downs:
+        inputs[v] = (rng.standard_normal(g.value_shape(v)) * 0.06).astype(np.float32)
+    sess = Session(g, device=rank, rank=rank, world=world, nccl_id=nccl_id)
+    for v, a in inputs.items():
+        sess.write(v, a)
+    sess.run()
+    got = sess.read(y).astype(np.float32)
+    plan = sess.plan
+    sess.close()
+    q.put((rank, plan.count("nccl_all_reduce")) + f16_close(got, oracle.evaluate(g, inputs)[y]))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_repeat_session_two_ranks():
+    import torch.multiprocessing as mp
+    from ipuc.graph import nccl_unique_id
+    nccl_id = nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_repeat_worker, args=(r, 2, nccl_id, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, reduces, ok, msg in res:
+        assert reduces == 3, f"rank {rank}: {reduces} all-reduces"
+        assert ok, f"rank {rank}: {msg}"

@@ -96,3 +96,20 @@ def test_sharded_block_sums_to_unsharded_block_gloo():
         assert p.exitcode == 0
     for _, err, scale in res:
         assert err <= 1e-5 * scale
+
+
+def test_graph_shard_matches_closed_form_plan():
+    """The sharded session's split, derived from the block's graph, is the
+    closed-form Megatron plan (ipuc.tp.plan) at every rank."""
+    from ipuc.tp import block_graph
+    d, H, ff = 1024, 16, 4096
+    g, x, w, y = block_graph(2, 128, d, H, ff)
+    for world in (2, 4, 8):
+        for rank in range(world):
+            sh = plan(d, H, ff, rank, world)
+            sl = {v["graph_value"]: v for v in g.shard(rank, world)["values"] if v["kind"] == 1}
+            for n in ("wq", "wk", "wv"):
+                assert (sl[w[n]]["slice"], tuple(sl[w[n]]["range"])) == ("columns", sh.qkv_cols)
+            assert (sl[w["wo"]]["slice"], tuple(sl[w["wo"]]["range"])) == ("rows", sh.qkv_cols)
+            assert (sl[w["w1"]]["slice"], tuple(sl[w["w1"]]["range"])) == ("columns", sh.ff_cols)
+            assert (sl[w["w2"]]["slice"], tuple(sl[w["w2"]]["range"])) == ("rows", sh.ff_cols)
