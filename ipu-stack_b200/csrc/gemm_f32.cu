@@ -257,7 +257,7 @@ constexpr int ROW_CACHE = 4;
 __global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                              int64_t ld, int32_t *__restrict__ rexp, int64_t ldp,
                                                              __half *__restrict__ hi, __half *__restrict__ lo,
-                                                             int32_t *__restrict__ tiny) {
+                                                             int32_t *__restrict__ tiny, uint32_t *__restrict__ fixrow) {
   __shared__ uint32_t red[8];
   __shared__ int cnt[8];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -295,7 +295,10 @@ __global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__rest
 #pragma unroll
     for (int w = 1; w < 8; ++w) mx = max(mx, red[w]);
     const int e = split_exponent(mx);
-    if (tid == 0) rexp[r] = e;
+    if (tid == 0) {
+      rexp[r] = e;
+      if (fixrow) fixrow[r] = 0u;  // the epilogue raises it where a row needs the fix-up
+    }
     const float scale = pow2(e);
     int t = 0;
 #pragma unroll
@@ -416,63 +419,103 @@ __device__ __forceinline__ float unscale(float v, int e_row, int e_col) {
   return (v * pow2(-e_row)) * pow2(-e_col);
 }
 
-__device__ __forceinline__ void mark_fixup(const Gemm32Params &p, int64_t row, int64_t col) {
-  atomicOr(p.fixmap + row * p.fix_words + (col >> 5), 1u << (col & 31));
-  p.fixrow[row] = 1u;
+// Writes one 32-column word of the fix-up bitmap (3xF16).  A whole tile's
+// epilogue owns its words, so it stores them outright (no clearing needed);
+// the two K halves of a split tile OR theirs into words the zeroing kernel
+// cleared.
+__device__ __forceinline__ void put_fix_word(const Gemm32Params &p, int64_t row, int64_t col, uint32_t word,
+                                             bool split) {
+  uint32_t *w = p.fixmap + row * p.fix_words + (col >> 5);
+  if (split) {
+    if (word) atomicOr(w, word);
+  } else {
+    *w = word;
+  }
+  if (word) p.fixrow[row] = 1u;
 }
 
 // Epilogue store of the scaled sums v of C[row][col .. col+3] (cp points at
 // C[row][col]): unscaled (3xF16), then added atomically (a K-split half),
-// added to C (IPUC_GEMM_ACCUMULATE) or stored; elements that need the fix-up
-// are left alone and marked.
+// added to C (IPUC_GEMM_ACCUMULATE) or stored.  Elements that need the fix-up
+// are left alone; the returned 4-bit mask names them.
 template <bool kF16>
-__device__ __forceinline__ void store_c4(const Gemm32Params &p, float *cp, int64_t row, int64_t col, float4 v, int er,
-                                         int tr, bool split, bool accumulate) {
+__device__ __forceinline__ uint32_t store_c4(const Gemm32Params &p, float *cp, int64_t col, float4 v, int er, int tr,
+                                             bool split, bool accumulate) {
   if constexpr (kF16) {
     const int4 ec = __ldg(reinterpret_cast<const int4 *>(p.eb + col));
     const int4 tc = __ldg(reinterpret_cast<const int4 *>(p.tb + col));
-    const bool f0 = needs_fixup(v.x, tr + tc.x), f1 = needs_fixup(v.y, tr + tc.y);
-    const bool f2 = needs_fixup(v.z, tr + tc.z), f3 = needs_fixup(v.w, tr + tc.w);
+    const uint32_t f = (needs_fixup(v.x, tr + tc.x) ? 1u : 0u) | (needs_fixup(v.y, tr + tc.y) ? 2u : 0u) |
+                       (needs_fixup(v.z, tr + tc.z) ? 4u : 0u) | (needs_fixup(v.w, tr + tc.w) ? 8u : 0u);
     v.x = unscale(v.x, er, ec.x);
     v.y = unscale(v.y, er, ec.y);
     v.z = unscale(v.z, er, ec.z);
     v.w = unscale(v.w, er, ec.w);
-    if (f0 | f1 | f2 | f3) {
+    if (f) {
       const float x[4] = {v.x, v.y, v.z, v.w};
-      const bool f[4] = {f0, f1, f2, f3};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        if (f[e]) mark_fixup(p, row, col + e);
-        else if (split) atomicAdd(cp + e, x[e]);
+        if (f & (1u << e)) continue;
+        if (split) atomicAdd(cp + e, x[e]);
         else cp[e] = accumulate ? cp[e] + x[e] : x[e];
       }
-      return;
+      return f;
     }
   }
   float4 *c4 = reinterpret_cast<float4 *>(cp);
   if (split) {
     atomicAdd(c4, v);
-    return;
+    return 0u;
   }
   if (accumulate) {
     const float4 o = *c4;
     v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
   }
   *c4 = v;
+  return 0u;
 }
 
 template <bool kF16>
-__device__ __forceinline__ void store_c1(const Gemm32Params &p, float *cp, int64_t row, int64_t col, float x, int er,
-                                         int tr, bool split, bool accumulate) {
+__device__ __forceinline__ uint32_t store_c1(const Gemm32Params &p, float *cp, int64_t col, float x, int er, int tr,
+                                             bool split, bool accumulate) {
   if constexpr (kF16) {
-    if (needs_fixup(x, tr + p.tb[col])) {
-      mark_fixup(p, row, col);
-      return;
-    }
+    if (needs_fixup(x, tr + p.tb[col])) return 1u;
     x = unscale(x, er, p.eb[col]);
   }
   if (split) atomicAdd(cp, x);
   else *cp = accumulate ? *cp + x : x;
+  return 0u;
+}
+
+// The epilogue of one thread's row segment (BN / 2 columns from col_base).
+template <bool kF16>
+__device__ __forceinline__ void store_row(const Gemm32Params &p, const float (&acc)[BN / 2], int64_t row,
+                                          int64_t col_base, bool vec_ok, bool split, bool accumulate) {
+  const int er = kF16 ? p.ea[row] : 0, tr = kF16 ? p.ta[row] : 0;
+  float *cp = p.c + row * p.ldc + col_base;
+  uint32_t word = 0;
+  if (vec_ok && col_base + BN / 2 <= p.n) {
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+      word |= store_c4<kF16>(p, cp + 4 * j, col_base + 4 * j,
+                             make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]), er, tr, split,
+                             accumulate)
+              << ((4 * j) & 31);
+      if (kF16 && (4 * j + 4) % 32 == 0) {
+        put_fix_word(p, row, col_base + 4 * j - 28, word, split);
+        word = 0;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) {
+      if (col_base + j < p.n)
+        word |= store_c1<kF16>(p, cp + j, col_base + j, acc[j], er, tr, split, accumulate) << (j & 31);
+      if (kF16 && (j & 31) == 31) {
+        if (col_base + j - 31 < p.n) put_fix_word(p, row, col_base + j - 31, word, split);
+        word = 0;
+      }
+    }
+  }
 }
 
 __device__ __forceinline__ void tile_coords(const Gemm32Params &p, int64_t t, int &mt, int &nt) {
@@ -497,14 +540,18 @@ __device__ __forceinline__ WorkUnit work_unit(const Gemm32Params &p, int64_t u, 
   return {p.split_from + v / 2, (v & 1) ? mid : 0, (v & 1) ? chunks : mid, true};
 }
 
-// Zeroes the C regions of the split tiles (blockIdx.y = tile - split_from).
+// Zeroes the C regions of the split tiles (blockIdx.y = tile - split_from)
+// and, for 3xF16, their words of the fix-up bitmap (the two halves OR into them).
 __global__ void __launch_bounds__(256) zero_split_tiles_kernel(const Gemm32Params p, int pair_bm) {
   int mt, nt;
   tile_coords(p, p.split_from + blockIdx.y, mt, nt);
   const int64_t r0 = (int64_t)mt * pair_bm, c0 = (int64_t)nt * BN;
   for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < pair_bm * BN; idx += gridDim.x * blockDim.x) {
     const int64_t r = r0 + idx / BN, c = c0 + idx % BN;
-    if (r < p.m && c < p.n) p.c[r * p.ldc + c] = 0.0f;
+    if (r < p.m && c < p.n) {
+      p.c[r * p.ldc + c] = 0.0f;
+      if (p.fixmap && (c & 31) == 0) p.fixmap[r * p.fix_words + (c >> 5)] = 0u;
+    }
   }
 }
 
@@ -669,21 +716,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, t, mt, nt);
       const int64_t row = (int64_t)mt * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
-      if (row < p.m) {
-        const int er = kF16 ? p.ea[row] : 0, tr = kF16 ? p.ta[row] : 0;
-        float *cp = p.c + row * p.ldc + col_base;
-        if (vec_ok && col_base + BN / 2 <= p.n) {
-#pragma unroll
-          for (int j = 0; j < BN / 8; ++j)
-            store_c4<kF16>(p, cp + 4 * j, row, col_base + 4 * j,
-                           make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]), er, tr, false,
-                           accumulate);
-        } else {
-#pragma unroll
-          for (int j = 0; j < BN / 2; ++j)
-            if (col_base + j < p.n) store_c1<kF16>(p, cp + j, row, col_base + j, acc[j], er, tr, false, accumulate);
-        }
-      }
+      if (row < p.m) store_row<kF16>(p, acc, row, col_base, vec_ok, false, accumulate);
     }
     if (!ok) {
       record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_EPILOGUE);
@@ -865,22 +898,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, w.tile, mt, nt);
       const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
       const int64_t col_base = (int64_t)nt * BN + half * (BN / 2);
-      if (row < p.m) {
-        const int er = kF16 ? p.ea[row] : 0, tr = kF16 ? p.ta[row] : 0;
-        float *cp = p.c + row * p.ldc + col_base;
-        if (vec_ok && col_base + BN / 2 <= p.n) {
-#pragma unroll
-          for (int j = 0; j < BN / 8; ++j)
-            store_c4<kF16>(p, cp + 4 * j, row, col_base + 4 * j,
-                           make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]), er, tr, w.split,
-                           accumulate);
-        } else {
-#pragma unroll
-          for (int j = 0; j < BN / 2; ++j)
-            if (col_base + j < p.n)
-              store_c1<kF16>(p, cp + j, row, col_base + j, acc[j], er, tr, w.split, accumulate);
-        }
-      }
+      if (row < p.m) store_row<kF16>(p, acc, row, col_base, vec_ok, w.split, accumulate);
     }
     if (!ok) {
       record_device_error(p.err, ERR_KERNEL_GEMM_F32 | ERR_SITE_EPILOGUE);
@@ -1059,10 +1077,11 @@ ipuc_status gemm_f32_launch(float *c, const float *a, const float *b, int64_t m,
     int32_t *ta = reinterpret_cast<int32_t *>(mbase + m4 + 3 * n4);
     uint32_t *fixrow = reinterpret_cast<uint32_t *>(mbase + 2 * m4 + 3 * n4);
     uint32_t *fixmap = reinterpret_cast<uint32_t *>(mbase + 3 * m4 + 3 * n4);
-    IPUC_CUDA(cudaMemsetAsync(fixrow, 0, m4 + round256((uint64_t)m * words * 4), stream));
-    split_f16_rows_kernel<<<(unsigned)(m < cap ? m : cap), 256, 0, stream>>>(a, m, k, lda, ea, kp, ah, al, ta);
+    split_f16_rows_kernel<<<(unsigned)(m < cap ? m : cap), 256, 0, stream>>>(a, m, k, lda, ea, kp, ah, al, ta,
+                                                                               fixrow);
     if (bt) {
-      split_f16_rows_kernel<<<(unsigned)(n < cap ? n : cap), 256, 0, stream>>>(b, n, k, ldb, eb, kp, bh, bl, tb);
+      split_f16_rows_kernel<<<(unsigned)(n < cap ? n : cap), 256, 0, stream>>>(b, n, k, ldb, eb, kp, bh, bl, tb,
+                                                                               nullptr);
     } else {
       IPUC_CUDA(cudaMemsetAsync(bmax, 0, 2 * n4, stream));
       const int64_t col_ctas = ((n + 127) / 128) * ((k + COLMAX_ROWS - 1) / COLMAX_ROWS);

@@ -75,6 +75,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
+// Programmatic dependent launch: a grid launched with the programmatic
+// stream-serialization attribute may start before the previous kernel in the
+// stream has finished; griddep_wait blocks until that kernel has completed
+// and its memory is visible (it returns at once when there is none), and
+// griddep_launch_dependents lets the next such grid start its prologue.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named CTA barrier over `count` threads (count a multiple of 32).
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -179,3 +179,30 @@ def test_gemm_a_transposed_batched_gelu():
                           flags=ipuc.GEMM_A_TRANSPOSED | ipuc.GEMM_EPILOGUE_GELU)
     ok, msg = f16_close(f16_of(host_u16(c)).reshape(batch, m, n), ref)
     assert ok, msg
+
+
+@pytest.mark.parametrize("flags,with_c", [(0, False), (ipuc.GEMM_EPILOGUE_GELU, False), (ipuc.GEMM_OUT_F32, False),
+                                          (ipuc.GEMM_ACCUMULATE, True), (ipuc.GEMM_B_TRANSPOSED, False)])
+def test_gemm_split_tail_wave(flags, with_c):
+    """80 pair tiles (2048 x 2560) on the CTA-pair kernel: the last, partial
+    wave runs each tile as two K halves that hand off through C (not when C is
+    the accumulation source)."""
+    got, ref = run_case(2048, 2560, 1024, flags, seed=77 + flags, with_c=with_c)
+    ok, msg = f16_close(got, ref)
+    assert ok, msg
+
+
+def test_gemm_split_tail_with_addend():
+    """gemm_f16_addend (C = A.B + D, D separate) with the split tail, twice in a
+    row (the hand-off flags are tagged per launch)."""
+    m, n, k = 2048, 2560, 1024
+    a = oracle.f16_bits(seeded_normal(91, (m, k), 0.1))
+    b = oracle.f16_bits(seeded_normal(92, (k, n), 0.1))
+    d = oracle.f16_bits(seeded_normal(93, (m, n)))
+    ref = oracle.quantize_f16(oracle.gemm(f16_of(a), f16_of(b)) + f16_of(d))
+    for _ in range(2):
+        c = empty_u16(m * n)
+        ipuc.gemm_f16_addend(c, dev_u16(a), dev_u16(b), m, n, k, dev_u16(d))
+        ok, msg = f16_close(f16_of(host_u16(c)).reshape(m, n), ref)
+        assert ok, msg
+    ipuc.device_status()
