@@ -349,6 +349,11 @@ def run_ours(args):
         achieved = dom_flop / (dom_ms * 1e-3) / 1e12
         gemm_tf = GEMM_FLOP * nw / MLP_N / (gemm_ms * 1e-3) / 1e12
         attn_tf = ATT_FLOP * ns / (ATT_B * ATT_H) / (attn_ms * 1e-3) / 1e12
+        if "shard8" in comps and world == 1:
+            # the N=8 shards' per-GPU rate as a fraction of the full-size kernels' rate
+            comps["shard8"]["gemm_f16_gelu"]["of_full"] = round(comps["shard8"]["gemm_f16_gelu"]["tflops"] / gemm_tf, 3)
+            comps["shard8"]["flash_attention"]["of_full"] = round(comps["shard8"]["flash_attention"]["tflops"] / attn_tf,
+                                                                  3)
         # The burst peak applies to a timed region shorter than the seconds-long
         # loop the sustained figure was measured with; 2 s or more of timed
         # work is held against the sustained (power-capped) peak.
@@ -583,8 +588,47 @@ def measure_components(ipuc, torch, stream, hbm_gbs):
         out["gemm_f32_4096"] = {"unavailable": str(e)}
     del a32, b32, c32, ws
     torch.cuda.empty_cache()
+    out["shard8"] = shard8_kernels(ipuc, torch, stream)
     out["gemm_f16_256"] = gemm_f16_small(ipuc, torch, stream)
     out["transformer_block"] = transformer_block(ipuc, torch, stream)
+    return out
+
+
+def shard8_kernels(ipuc, torch, stream):
+    """The per-GPU shards of the headline step at N=8, timed on this GPU: the
+    GEMM column shard 8192x2048x4096 + GELU (256 pair tiles on 74 pair slots:
+    3.46 waves, the last one run as K halves) and the attention shard of 32
+    streams (its tail as split clusters).  TFLOP/s per GPU, to set beside the
+    full-size kernels' rates (kernels.*.tflops) as the N=8 per-GPU efficiency."""
+    s = stream.cuda_stream
+    m, n, k = MLP_M, MLP_N // 8, MLP_K
+    x = torch.randn((m, k), device="cuda").half()
+    w = (torch.randn((k, n), device="cuda") / 64).half()
+    y = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    M = ATT_B * ATT_H // 8
+    q, kk, v = (torch.randn((M, ATT_S, ATT_D), device="cuda").half() for _ in range(3))
+    o = torch.empty_like(q)
+    cases = {
+        "gemm_f16_gelu": (2.0 * m * n * k, lambda: ipuc.call("ipuc_gemm_f16", y.data_ptr(), x.data_ptr(), w.data_ptr(),
+                                                               m, n, k, k, n, n, ipuc.GEMM_EPILOGUE_GELU, s)),
+        "flash_attention": (ATT_FLOP / 8, lambda: ipuc.call("ipuc_flash_attention_f16", o.data_ptr(), ipuc.F16,
+                                                             q.data_ptr(), kk.data_ptr(), v.data_ptr(), M, ATT_S,
+                                                             ATT_S, ATT_D, 0.0, s)),
+    }
+    out = {}
+    for name, (flop, fn) in cases.items():
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record(stream)
+        for _ in range(20):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / 20
+        out[name] = {"ms": round(ms, 4), "tflops": round(flop / (ms * 1e-3) / 1e12, 1)}
+    del x, w, y, q, kk, v, o
+    torch.cuda.empty_cache()
     return out
 
 

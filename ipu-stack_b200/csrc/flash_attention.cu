@@ -22,9 +22,13 @@
 // Head dims up to 128 (multiple of 8) are zero-padded to 128 by the TMA; key
 // and query tails are masked.  Every wait is bounded (error word, no trap).
 //
-// Launch partition: from 512 query rows up, CTA pairs (cta_group::2, M = 256
-// over the pair, each CTA loading half of every K and V tile) take 512-row
-// units in whole waves; a last wave at most half full runs as split clusters
+// Launch partition: from 512 query rows up, persistent CTA pairs
+// (cta_group::2, M = 256 over the pair, each CTA loading half of every K and
+// V tile) loop over 512-row units in whole waves: the next unit's Q lands in
+// a second Q buffer while the current unit runs, and its first QK^T products
+// queue behind the current unit's last PV products while the softmax warps
+// store the finished O (the first PV of a unit waits until O is read out);
+// a last wave at most half full runs as split clusters
 // (kSplit: two CTAs per 256-row unit, each over half the key tiles, merged
 // through distributed shared memory).  Q/K/V/O are addressed through 4-D maps
 // (head_dim, heads, rows, batch), so the same kernels serve [streams][rows][d]
@@ -61,6 +65,7 @@ struct AttnParams {
   int32_t heads;      // streams per batch entry: Q/K/V/O are [batch][rows][heads * d] (1: [streams][rows][d])
   int32_t q_units;    // query units per stream: 512-row (pair, split) or 256-row blocks
   int64_t unit_base;  // first unit of this launch (split: first 256-row half-unit)
+  int64_t num_units;  // pair launch: units [unit_base, unit_base + num_units), looped over by persistent pairs
   uint32_t *err;
 };
 
@@ -81,63 +86,89 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                            const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sQ = smem;                       // Q0, Q1
-  uint8_t *sK = smem + 2 * TILE_BYTES;      // 2 stages
-  uint8_t *sV = smem + 4 * TILE_BYTES;      // 2 stages
+  constexpr int K_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA K tile (64 or 128 keys)
+  constexpr int K_HALF = K_BYTES / 2;                             // one 64-column head-dim half
+  constexpr int V_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA V tile (64 or 128 D columns)
+  constexpr int TX_MULT = kPair ? 2 : 1;                          // leader counts both CTAs' bytes
+  // Shared memory: Q buffers (two in the persistent pair kernel, so the next
+  // unit's Q lands while this one runs), then the K and V stage rings.
+  uint8_t *sQ0 = smem;
+  uint8_t *sQ1 = smem + (kPair ? 2 * TILE_BYTES : 0);
+  uint8_t *sK = smem + (kPair ? 4 : 2) * TILE_BYTES;  // 2 stages of K_BYTES
+  uint8_t *sV = sK + 2 * K_BYTES;                      // 2 stages of V_BYTES
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * TILE_BYTES);
-  uint64_t *q_full = bars + 0;
-  uint64_t *k_full = bars + 1;   // [2]
-  uint64_t *v_full = bars + 3;   // [2]
-  uint64_t *k_empty = bars + 5;  // [2] K stage free (its QK^T products done)
-  uint64_t *s_full = bars + 7;   // [2] per Q tile
-  uint64_t *p_ready = bars + 9;  // [2] per Q tile
-  uint64_t *o_final = bars + 11;
-  uint64_t *v_empty = bars + 12; // [2] V stage free (its PV products done)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+  uint64_t *q_full = bars + 0;   // [2] per Q buffer
+  uint64_t *k_full = bars + 2;   // [2]
+  uint64_t *v_full = bars + 4;   // [2]
+  uint64_t *k_empty = bars + 6;  // [2] K stage free (its QK^T products done)
+  uint64_t *s_full = bars + 8;   // [2] per Q tile
+  uint64_t *p_ready = bars + 10; // [2] per Q tile
+  uint64_t *o_final = bars + 12; // a unit's last PV products done
+  uint64_t *v_empty = bars + 13; // [2] V stage free (its PV products done)
+  uint64_t *q_empty = bars + 15; // [2] Q buffer free (its unit's QK^T products done)
+  uint64_t *o_empty = bars + 17; // [2] per Q tile: the unit's O read out, the next unit may overwrite it
+  uint64_t *merge_ready = bars + 19;  // split, CTA 1: CTA 0's tiles are free to receive
+  uint64_t *merge_full = bars + 20;   // split, CTA 0: CTA 1's partial has landed
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 21);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  uint64_t *merge_ready = bars + 15;  // split, CTA 1: CTA 0's tiles are free to receive
-  uint64_t *merge_full = bars + 16;   // split, CTA 0: CTA 1's partial has landed
 
   __shared__ float xmax[2][2][TQ], xsum[2][2][TQ];  // [tile][column half][row]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = (kPair || kSplit) ? cluster_ctarank() : 0u;
   const uint32_t prank = kPair ? rank : 0u;  // half of K/V this CTA loads (pair only)
   const bool leader = prank == 0;
-  int64_t stream;
-  int32_t q0;
+  // Units this CTA runs: the persistent pair kernel loops over pair units
+  // (512 query rows each); the single and split kernels run one unit per CTA.
+  // (unit indices fit 32 bits: streams < 2^24, units per stream < 2^22)
+  int32_t u_first, u_step, u_end;
   if (kPair) {
-    const int64_t u = p.unit_base + (blockIdx.x >> 1);
-    stream = u / p.q_units;
-    q0 = (int32_t)(u % p.q_units) * (4 * TQ) + (int32_t)rank * (2 * TQ);
-  } else if (kSplit) {
-    const int64_t u = p.unit_base + (blockIdx.x >> 1), pu = u >> 1;
-    stream = pu / p.q_units;
-    q0 = (int32_t)(pu % p.q_units) * (4 * TQ) + (int32_t)(u & 1) * (2 * TQ);
+    u_first = (int32_t)p.unit_base + (int32_t)(blockIdx.x >> 1);
+    u_step = (int32_t)(gridDim.x >> 1);
+    u_end = (int32_t)(p.unit_base + p.num_units);
   } else {
-    const int64_t u = p.unit_base + blockIdx.x;
-    stream = u / p.q_units;
-    q0 = (int32_t)(u % p.q_units) * (2 * TQ);
+    u_first = (int32_t)p.unit_base + (int32_t)(kSplit ? (blockIdx.x >> 1) : blockIdx.x);
+    u_step = 1;
+    u_end = u_first + 1;
   }
-  constexpr int K_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA K tile (64 or 128 keys)
-  constexpr int K_HALF = K_BYTES / 2;                             // one 64-column head-dim half
-  constexpr int V_BYTES = kPair ? TILE_BYTES / 2 : TILE_BYTES;   // per-CTA V tile (64 or 128 D columns)
-  constexpr int TX_MULT = kPair ? 2 : 1;                          // leader counts both CTAs' bytes
-  const int32_t s_head = (int32_t)(stream % p.heads), s_batch = (int32_t)(stream / p.heads);
+  struct Unit {
+    int64_t stream;
+    int32_t q0, s_head, s_batch;
+    int j_begin, n_tiles;
+  };
   // Key tiles [j_begin, j_begin + n_tiles) of the stream; loop counters below
   // are local (they set stage and phase), key coordinates add j_begin.
-  const int split_half = (p.key_tiles + 1) / 2;
-  const int j_begin = kSplit ? (int)rank * split_half : 0;
-  const int n_tiles = kSplit ? min(p.key_tiles - j_begin, split_half) : p.key_tiles;
+  auto decode = [&](int32_t u) {
+    Unit w;
+    if (kPair) {
+      w.stream = u / p.q_units;
+      w.q0 = (int32_t)(u % p.q_units) * (4 * TQ) + (int32_t)rank * (2 * TQ);
+    } else if (kSplit) {
+      const int32_t pu = u >> 1;
+      w.stream = pu / p.q_units;
+      w.q0 = (int32_t)(pu % p.q_units) * (4 * TQ) + (int32_t)(u & 1) * (2 * TQ);
+    } else {
+      w.stream = u / p.q_units;
+      w.q0 = (int32_t)(u % p.q_units) * (2 * TQ);
+    }
+    w.s_head = (int32_t)(w.stream % p.heads);
+    w.s_batch = (int32_t)(w.stream / p.heads);
+    const int split_half = (p.key_tiles + 1) / 2;
+    w.j_begin = kSplit ? (int)rank * split_half : 0;
+    w.n_tiles = kSplit ? min(p.key_tiles - w.j_begin, split_half) : p.key_tiles;
+    return w;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], kPair ? 16 : 8);  // lane 0 of each softmax warp of the tile
+      mbar_init(&o_empty[i], kPair ? 16 : 8);
     }
     mbar_init(o_final, 1);
     mbar_init(merge_ready, 1);
@@ -167,34 +198,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
-      auto load = [&](void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x, int32_t y) {
-        // 4-D maps (head_dim, heads, rows, batch): a stream is (batch, head).
-        if (kPair) tma_load_4d_pair(dst, map, bar, x, s_head, y, s_batch);
-        else tma_load_4d(dst, map, bar, x, s_head, y, s_batch);
-      };
-      if (leader) mbar_arrive_expect_tx(q_full, TX_MULT * 2 * TILE_BYTES);
-      for (int t = 0; t < 2; ++t)
-        for (int h = 0; h < 2; ++h) load(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, q_full, h * 64, q0 + t * TQ);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait_bounded(&k_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
+      uint32_t jg = 0;  // key tiles loaded so far (ring stage and phase)
+      int local = 0;
+      for (int32_t u = u_first; u < u_end && ok; u += u_step, ++local) {
+        const Unit w = decode(u);
+        auto load = [&](void *dst, const CUtensorMap *map, uint64_t *bar, int32_t x, int32_t y) {
+          // 4-D maps (head_dim, heads, rows, batch): a stream is (batch, head).
+          if (kPair) tma_load_4d_pair(dst, map, bar, x, w.s_head, y, w.s_batch);
+          else tma_load_4d(dst, map, bar, x, w.s_head, y, w.s_batch);
+        };
+        const int qb = local & 1;
+        uint8_t *sQ = qb ? sQ1 : sQ0;
+        // The Q buffer's previous unit (two back) has finished its QK^T products.
+        if (kPair && local >= 2 && !mbar_wait_bounded(&q_empty[qb], ((local >> 1) & 1) ^ 1, abort_flag)) {
           ok = false;
           break;
         }
-        if (leader) mbar_arrive_expect_tx(&k_full[st], TX_MULT * K_BYTES);
-        for (int h = 0; h < 2; ++h)
-          load(sK + st * TILE_BYTES + h * K_HALF, &tmK, &k_full[st], h * 64,
-               (j_begin + j) * TK + (int32_t)prank * (TK / 2));
-        if (!mbar_wait_bounded(&v_empty[st], ((j >> 1) & 1) ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        if (leader) mbar_arrive_expect_tx(&v_full[st], TX_MULT * V_BYTES);
-        if (kPair) {
-          load(sV + st * TILE_BYTES, &tmV, &v_full[st], (int32_t)prank * 64, (j_begin + j) * TK);
-        } else {
+        if (leader) mbar_arrive_expect_tx(&q_full[qb], TX_MULT * 2 * TILE_BYTES);
+        for (int t = 0; t < 2; ++t)
+          for (int h = 0; h < 2; ++h) load(sQ + t * TILE_BYTES + h * HALF_BYTES, &tmQ, &q_full[qb], h * 64, w.q0 + t * TQ);
+        for (int j = 0; j < w.n_tiles && ok; ++j, ++jg) {
+          const int st = jg & 1;
+          if (!mbar_wait_bounded(&k_empty[st], ((jg >> 1) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&k_full[st], TX_MULT * K_BYTES);
           for (int h = 0; h < 2; ++h)
-            load(sV + st * TILE_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, (j_begin + j) * TK);
+            load(sK + st * K_BYTES + h * K_HALF, &tmK, &k_full[st], h * 64,
+                 (w.j_begin + j) * TK + (int32_t)prank * (TK / 2));
+          if (!mbar_wait_bounded(&v_empty[st], ((jg >> 1) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&v_full[st], TX_MULT * V_BYTES);
+          if (kPair) {
+            load(sV + st * V_BYTES, &tmV, &v_full[st], (int32_t)prank * 64, (w.j_begin + j) * TK);
+          } else {
+            for (int h = 0; h < 2; ++h)
+              load(sV + st * V_BYTES + h * HALF_BYTES, &tmV, &v_full[st], h * 64, (w.j_begin + j) * TK);
+          }
         }
       }
       if (!ok) {
@@ -210,67 +253,85 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (kPair) mma_commit_pair(bar, 0x3);
         else mma_commit(bar);
       };
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
+      bool ok = true;
       // Descriptors are built once; each k-step adds a compile-time offset (in
       // 16-byte units) so the single issuing thread spends about one integer
       // add per MMA and keeps the tensor pipe fed.
-      const uint64_t q_desc = make_smem_desc(smem_u32(sQ), 16, 1024, kSwizzle128B);
       const uint64_t k_desc = make_smem_desc(smem_u32(sK), 16, 1024, kSwizzle128B);
       const uint64_t v_desc = make_smem_desc(smem_u32(sV), HALF_BYTES, 1024, kSwizzle128B);
-      auto issue_s = [&](int t, int stage) {
-        const uint64_t qd = q_desc + (uint64_t)(t * (TILE_BYTES >> 4));
-        const uint64_t kd = k_desc + (uint64_t)(stage * (TILE_BYTES >> 4));
-        const uint32_t d = tmem + t * 128;
+      uint32_t jg = 0;
+      int local = 0;
+      for (int32_t u = u_first; u < u_end && ok; u += u_step, ++local) {
+        const Unit w = decode(u);
+        const int qb = local & 1;
+        const uint64_t q_desc = make_smem_desc(smem_u32(qb ? sQ1 : sQ0), 16, 1024, kSwizzle128B);
+        auto issue_s = [&](int t, int stage) {
+          const uint64_t qd = q_desc + (uint64_t)(t * (TILE_BYTES >> 4));
+          const uint64_t kd = k_desc + (uint64_t)(stage * (K_BYTES >> 4));
+          const uint32_t d = tmem + t * 128;
 #pragma unroll
-        for (int k = 0; k < DP / 16; ++k) {
-          const uint64_t adesc = qd + (uint64_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
-          const uint64_t bdesc = kd + (uint64_t)(((k >> 2) * K_HALF + (k & 3) * 32) >> 4);
-          if (kPair) mma_f16_ss_pair(d, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
-          else mma_f16_ss(d, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+          for (int k = 0; k < DP / 16; ++k) {
+            const uint64_t adesc = qd + (uint64_t)(((k >> 2) * HALF_BYTES + (k & 3) * 32) >> 4);
+            const uint64_t bdesc = kd + (uint64_t)(((k >> 2) * K_HALF + (k & 3) * 32) >> 4);
+            if (kPair) mma_f16_ss_pair(d, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+            else mma_f16_ss(d, adesc, bdesc, idesc_s, k > 0 ? 1u : 0u);
+          }
+          commit(&s_full[t]);
+        };
+        // Issue order per key tile j (stage st):
+        //   [P_0(j)] PV_0(j), (release K stage of tile j after its last use)
+        //            S_0(j+1)
+        //   [P_1(j)] PV_1(j), release V stage st, [V(j+1) landed], S_1(j+1)
+        // The bookkeeping between S_1(j+1) and PV_0(j+1) -- when the tensor
+        // pipe may run dry -- is one commit and the P_0 wait.  A unit's first
+        // S products follow the previous unit's last PV products in the same
+        // pipe, so its S tiles (holding the last P) are free by then.
+        ok = mbar_wait_bounded(&q_full[qb], (local >> 1) & 1, abort_flag);
+        if (ok) ok = mbar_wait_bounded(&k_full[jg & 1], (jg >> 1) & 1, abort_flag);
+        if (ok) {
+          issue_s(0, jg & 1);
+          issue_s(1, jg & 1);
         }
-        commit(&s_full[t]);
-      };
-      // Issue order per key tile j (stage st = j & 1):
-      //   [P_0(j)] PV_0(j), (release K stage of tile j after its last use)
-      //            S_0(j+1)
-      //   [P_1(j)] PV_1(j), release V stage st, [V(j+1) landed], S_1(j+1)
-      // The bookkeeping between S_1(j+1) and PV_0(j+1) -- when the tensor
-      // pipe may run dry -- is one commit and the P_0 wait.
-      if (ok) ok = mbar_wait_bounded(&k_full[0], 0, abort_flag);
-      if (ok) {
-        issue_s(0, 0);
-        issue_s(1, 0);
-      }
-      if (ok) ok = mbar_wait_bounded(&v_full[0], 0, abort_flag);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j & 1;
-        const bool more = j + 1 < n_tiles;
-        const uint64_t vd = v_desc + (uint64_t)(st * (TILE_BYTES >> 4));
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (!mbar_wait_bounded(&p_ready[t], j & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d = tmem + 256 + t * 128, a = tmem + t * 128;
-          const uint32_t acc0 = j > 0 ? 1u : 0u;
+        if (ok) ok = mbar_wait_bounded(&v_full[jg & 1], (jg >> 1) & 1, abort_flag);
+        for (int j = 0; j < w.n_tiles && ok; ++j, ++jg) {
+          const int st = jg & 1;
+          const bool more = j + 1 < w.n_tiles;
+          const uint64_t vd = v_desc + (uint64_t)(st * (V_BYTES >> 4));
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!mbar_wait_bounded(&p_ready[t], jg & 1, abort_flag)) { ok = false; break; }
+            // The previous unit's epilogue has read O_t out before the first
+            // PV of this unit overwrites it.
+            if (kPair && j == 0 && local > 0 && !mbar_wait_bounded(&o_empty[t], (local - 1) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + 256 + t * 128, a = tmem + t * 128;
+            const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
-          for (int k = 0; k < TK / 16; ++k) {
-            // A = P_t (f16, 8 TMEM columns per 16 keys); B = V rows [16k, 16k+16)
-            const uint64_t bdesc = vd + (uint64_t)((k * 2048) >> 4);
-            if (kPair) mma_f16_ts_pair(d, a + k * 8, bdesc, idesc_o, k > 0 ? 1u : acc0);
-            else mma_f16_ts(d, a + k * 8, bdesc, idesc_o, k > 0 ? 1u : acc0);
+            for (int k = 0; k < TK / 16; ++k) {
+              // A = P_t (f16, 8 TMEM columns per 16 keys); B = V rows [16k, 16k+16)
+              const uint64_t bdesc = vd + (uint64_t)((k * 2048) >> 4);
+              if (kPair) mma_f16_ts_pair(d, a + k * 8, bdesc, idesc_o, k > 0 ? 1u : acc0);
+              else mma_f16_ts(d, a + k * 8, bdesc, idesc_o, k > 0 ? 1u : acc0);
+            }
+            if (t == 0) {
+              // K stage st was last read by S_1(j), complete before P_1(j) could
+              // have been produced; release it now that PV_0(j) is queued.
+              commit(&k_empty[st]);
+              if (more && !mbar_wait_bounded(&k_full[st ^ 1], ((jg + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+            } else {
+              commit(&v_empty[st]);
+              if (more && !mbar_wait_bounded(&v_full[st ^ 1], ((jg + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+            }
+            if (more) issue_s(t, st ^ 1);
           }
-          if (t == 0) {
-            // K stage st was last read by S_1(j), complete before P_1(j) could
-            // have been produced; release it now that PV_0(j) is queued.
-            commit(&k_empty[st]);
-            if (more && !mbar_wait_bounded(&k_full[st ^ 1], ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-          } else {
-            commit(&v_empty[st]);
-            if (more && !mbar_wait_bounded(&v_full[st ^ 1], ((j + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-          }
-          if (more) issue_s(t, st ^ 1);
+        }
+        if (ok) {
+          commit(o_final);
+          if (kPair) commit(&q_empty[qb]);
         }
       }
-      if (ok) commit(o_final);
       if (!ok) {
         record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_MMA);
         *abort_flag = 1;
@@ -292,116 +353,127 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t s_col = tmem + lane_off + t * 128;
     const uint32_t o_col = tmem + lane_off + 256 + t * 128 + h * 64;
     const float c = p.scale_log2;
-    float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait_bounded(&s_full[t], j & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      const int64_t rem_keys = p.sk - (int64_t)(j_begin + j) * TK - h * 64;
-      const int valid = rem_keys < 64 ? (rem_keys > 0 ? (int)rem_keys : 0) : 64;
-      // This warp's 64 scores stay in registers (P overwrites S columns of the
-      // partner's half only after the barrier below).
-      uint32_t a[32], b[32];
-      tmem_ld_32x32b_x32(s_col + h * 64, a);
-      tmem_ld_32x32b_x32(s_col + h * 64 + 32, b);
-      tmem_wait_ld(a);
-      tmem_regs_fence(b);
-      float mx = -INFINITY;
-      if (valid == 64) {
-        float mx1 = -INFINITY;
+    uint32_t jg = 0;
+    int local = 0;
+    for (int32_t u = u_first; u < u_end && ok; u += u_step, ++local) {
+      const int split_half = (p.key_tiles + 1) / 2;
+      const int j_begin = kSplit ? (int)rank * split_half : 0;
+      const int n_tiles = kSplit ? min(p.key_tiles - j_begin, split_half) : p.key_tiles;
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j < n_tiles; ++j, ++jg) {
+        if (!mbar_wait_bounded(&s_full[t], jg & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const int64_t rem_keys = p.sk - (int64_t)(j_begin + j) * TK - h * 64;
+        const int valid = rem_keys < 64 ? (rem_keys > 0 ? (int)rem_keys : 0) : 64;
+        // This warp's 64 scores stay in registers (P overwrites S columns of the
+        // partner's half only after the barrier below).
+        uint32_t a[32], b[32];
+        tmem_ld_32x32b_x32(s_col + h * 64, a);
+        tmem_ld_32x32b_x32(s_col + h * 64 + 32, b);
+        tmem_wait_ld(a);
+        tmem_regs_fence(b);
+        float mx = -INFINITY;
+        if (valid == 64) {
+          float mx1 = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(a[i + 1]));
-          mx1 = max3(mx1, __uint_as_float(a[i + 2]), __uint_as_float(a[i + 3]));
-          mx = max3(mx, __uint_as_float(b[i]), __uint_as_float(b[i + 1]));
-          mx1 = max3(mx1, __uint_as_float(b[i + 2]), __uint_as_float(b[i + 3]));
+          for (int i = 0; i < 32; i += 4) {
+            mx = max3(mx, __uint_as_float(a[i]), __uint_as_float(a[i + 1]));
+            mx1 = max3(mx1, __uint_as_float(a[i + 2]), __uint_as_float(a[i + 3]));
+            mx = max3(mx, __uint_as_float(b[i]), __uint_as_float(b[i + 1]));
+            mx1 = max3(mx1, __uint_as_float(b[i + 2]), __uint_as_float(b[i + 3]));
+          }
+          mx = fmaxf(mx, mx1);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i >= valid) a[i] = __float_as_uint(-INFINITY);
+            if (i + 32 >= valid) b[i] = __float_as_uint(-INFINITY);
+            mx = fmaxf(mx, fmaxf(__uint_as_float(a[i]), __uint_as_float(b[i])));
+          }
         }
-        mx = fmaxf(mx, mx1);
-      } else {
+        xmax[t][h][row] = mx;
+        named_barrier_sync(bar_id, 64);
+        mx = fmaxf(mx, xmax[t][h ^ 1][row]);
+        const float m_new = fmaxf(m, mx);
+        bool rescale = false;
+        float alpha = 1.0f;
+        if (j == 0) {
+          m = m_new;
+        } else if ((m_new - m) * c > RESCALE_THRESHOLD) {
+          alpha = ex2_approx((m - m_new) * c);
+          rescale = true;
+          m = m_new;
+          l *= alpha;
+        }
+        // P = 2^(s*c - m*c) in packed f16 written to S columns [h*32, h*32+32):
+        // packed f32x2 arithmetic, one pair in three exponentiated on the FMA
+        // pipe (exp2_poly2) to unload the MUFU unit (16 ex2 per clock per SM;
+        // a third on the polynomial balances it against the FMA pipe).  Masked
+        // keys hold -inf -> 0.
+        const float mc = m * c;
+        const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
+        uint64_t sum2 = f2_pack(0.0f, 0.0f);
+        uint32_t packed[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          if (i >= valid) a[i] = __float_as_uint(-INFINITY);
-          if (i + 32 >= valid) b[i] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, fmaxf(__uint_as_float(a[i]), __uint_as_float(b[i])));
+          const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
+          const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
+          const uint64_t tt = f2_fma(f2_pack(x0, x1), c2, nmc2);
+          uint64_t pp;
+          if ((i % 3) == 2) {
+            pp = exp2_poly2(tt);
+          } else {
+            float t0, t1;
+            f2_unpack(tt, t0, t1);
+            pp = f2_pack(ex2_approx(t0), ex2_approx(t1));
+          }
+          sum2 = f2_add(sum2, pp);
+          float p0, p1;
+          f2_unpack(pp, p0, p1);
+          __half2 h2 = __floats2half2_rn(p0, p1);
+          packed[i] = *reinterpret_cast<uint32_t *>(&h2);
+        }
+        tmem_st_32x32b_x32(s_col + h * 32, packed);
+        float s0, s1;
+        f2_unpack(sum2, s0, s1);
+        l += s0 + s1;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O_t is stable: PV_t(j-1) was issued before S_t(j), whose completion
+          // we observed.  Each warp rescales its 64 columns of O.
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(o_col + ch * 32, o);
+            tmem_wait_ld(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(o_col + ch * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (kPair) mbar_arrive_leader(&p_ready[t]);
+          else mbar_arrive(&p_ready[t]);
         }
       }
-      xmax[t][h][row] = mx;
+      if (!ok) break;
+      // Epilogue: combine the two partial row sums, then O_t / l -> out for this
+      // warp's 64 columns.
+      xsum[t][h][row] = l;
       named_barrier_sync(bar_id, 64);
-      mx = fmaxf(mx, xmax[t][h ^ 1][row]);
-      const float m_new = fmaxf(m, mx);
-      bool rescale = false;
-      float alpha = 1.0f;
-      if (j == 0) {
-        m = m_new;
-      } else if ((m_new - m) * c > RESCALE_THRESHOLD) {
-        alpha = ex2_approx((m - m_new) * c);
-        rescale = true;
-        m = m_new;
-        l *= alpha;
+      l += xsum[t][h ^ 1][row];
+      if (!mbar_wait_bounded(o_final, local & 1, abort_flag)) {
+        ok = false;
+        break;
       }
-      // P = 2^(s*c - m*c) in packed f16 written to S columns [h*32, h*32+32):
-      // packed f32x2 arithmetic, one pair in three exponentiated on the FMA
-      // pipe (exp2_poly2) to unload the MUFU unit (16 ex2 per clock per SM;
-      // a third on the polynomial balances it against the FMA pipe).  Masked
-      // keys hold -inf -> 0.
-      const float mc = m * c;
-      const uint64_t c2 = f2_pack(c, c), nmc2 = f2_pack(-mc, -mc);
-      uint64_t sum2 = f2_pack(0.0f, 0.0f);
-      uint32_t packed[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float x0 = __uint_as_float(i < 16 ? a[2 * i] : b[2 * i - 32]);
-        const float x1 = __uint_as_float(i < 16 ? a[2 * i + 1] : b[2 * i - 31]);
-        const uint64_t tt = f2_fma(f2_pack(x0, x1), c2, nmc2);
-        uint64_t pp;
-        if ((i % 3) == 2) {
-          pp = exp2_poly2(tt);
-        } else {
-          float t0, t1;
-          f2_unpack(tt, t0, t1);
-          pp = f2_pack(ex2_approx(t0), ex2_approx(t1));
-        }
-        sum2 = f2_add(sum2, pp);
-        float p0, p1;
-        f2_unpack(pp, p0, p1);
-        __half2 h2 = __floats2half2_rn(p0, p1);
-        packed[i] = *reinterpret_cast<uint32_t *>(&h2);
-      }
-      tmem_st_32x32b_x32(s_col + h * 32, packed);
-      float s0, s1;
-      f2_unpack(sum2, s0, s1);
-      l += s0 + s1;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // O_t is stable: PV_t(j-1) was issued before S_t(j), whose completion
-        // we observed.  Each warp rescales its 64 columns of O.
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(o_col + ch * 32, o);
-          tmem_wait_ld(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st_32x32b_x32(o_col + ch * 32, o);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (kPair) mbar_arrive_leader(&p_ready[t]);
-        else mbar_arrive(&p_ready[t]);
-      }
-    }
-    // Epilogue: combine the two partial row sums, then O_t / l -> out for this
-    // warp's 64 columns.
-    xsum[t][h][row] = l;
-    named_barrier_sync(bar_id, 64);
-    l += xsum[t][h ^ 1][row];
-    if (ok && mbar_wait_bounded(o_final, 0, abort_flag)) {
       tc_fence_after();
-      const int64_t grow = (int64_t)q0 + t * TQ + row;
+      const Unit w = decode(u);
+      const int64_t grow = (int64_t)w.q0 + t * TQ + row;
       const bool row_ok = grow < p.sq;
-      const int64_t base = ((s_batch * p.sq + grow) * p.heads + s_head) * p.d;
+      const int64_t base = ((w.s_batch * p.sq + grow) * p.heads + w.s_head) * p.d;
       // Split merge area in CTA 0: its Q/K/V tiles, dead once its MMAs are
       // complete.  Rows are padded to RECV_LD floats so that one warp's
       // float4 reads of 32 rows spread over all banks.
@@ -456,6 +528,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(o_col + ch * 32, r);
         tmem_wait_ld(r);
+        if (kPair && ch == 1) {
+          // O_t is read out: the next unit's first PV may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_leader(&o_empty[t]);
+        }
         if (kSplit) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
@@ -486,8 +564,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
-    } else if (ok) {
-      ok = false;
+      if (kPair && !store) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_leader(&o_empty[t]);
+      }
     }
     if (!ok) {
       record_device_error(p.err, ERR_KERNEL_ATTENTION | ERR_SITE_EPILOGUE);
@@ -556,6 +637,7 @@ ipuc_status attention_launch(void *out, ipuc_precision out_precision, const void
   p.key_tiles = (int32_t)((key_rows + TK - 1) / TK);
   p.heads = (int32_t)heads;
   p.unit_base = 0;
+  p.num_units = 0;
   p.err = device_error_word();
   auto launch = [&](auto kernel, int64_t ctas, bool cluster, const CUtensorMap &kmap) -> ipuc_status {
     IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -587,7 +669,10 @@ ipuc_status attention_launch(void *out, ipuc_precision out_precision, const void
   const bool split = tail > 0 && 4 * tail <= 2 * slots && p.key_tiles >= 2;
   const int64_t paired = split ? full : units;
   if (paired > 0) {
-    st = launch(flash_attention_kernel<true, false>, 2 * paired, true, tk);
+    // persistent pairs: each loops over pair units (the next unit's Q and the
+    // previous unit's O store overlap this unit's products)
+    p.num_units = paired;
+    st = launch(flash_attention_kernel<true, false>, 2 * (paired < slots ? paired : slots), true, tk);
     if (st != IPUC_OK) return st;
   }
   if (!split) return IPUC_OK;

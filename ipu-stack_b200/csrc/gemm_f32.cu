@@ -186,7 +186,10 @@ __device__ __forceinline__ float pow2(int e) { return __uint_as_float((uint32_t)
 constexpr int32_t kTinyAll = 1 << 24;           // tiny count of a row/column with a non-finite value
 __device__ __forceinline__ uint32_t abs_bits(float x) { return __float_as_uint(x) & 0x7fffffffu; }
 // A scaled element that keeps fewer than 22 bits in hi + lo.
-__device__ __forceinline__ int is_tiny(float xs) { return xs != 0.0f && fabsf(xs) < 0.125f; }
+// (|xs| bits - 1) < bits(0.125) - 1 as unsigned: nonzero and below 2^-3.
+__device__ __forceinline__ int is_tiny(float xs) {
+  return ((__float_as_uint(xs) & 0x7fffffffu) - 1u) < 0x3dffffffu;
+}
 // True where the tiny elements of the element's row and column (`tiny`
 // together) may have moved the scaled sum v by more than 2^-23 |v| (or v is
 // not finite while a non-finite input is involved).
@@ -363,8 +366,8 @@ __global__ void __launch_bounds__(256) split_f16_transpose_kernel(const float *_
     for (int i = 0; i < 4; ++i) {
       const int oc = ty + 16 * i, orr = tx * 4;  // plane row = source column c0 + oc
       const int64_t c = c0 + oc, r = r0 + orr;
-      int t = 0;
       if (c < cols && r < ldp) {
+        int t = 0;
         const uint32_t mx = cmax[c];
         const int ce = split_exponent(mx);
         if (r0 == 0 && tx == 0) {
@@ -381,12 +384,9 @@ __global__ void __launch_bounds__(256) split_f16_transpose_kernel(const float *_
         }
         *reinterpret_cast<uint2 *>(hi + c * ldp + r) = *reinterpret_cast<const uint2 *>(h);
         *reinterpret_cast<uint2 *>(lo + c * ldp + r) = *reinterpret_cast<const uint2 *>(l);
-        if (mx >= 0x7f800000u) t = 0;  // the column is marked whole
+        // tiny elements are rare: one atomic where a thread holds some
+        if (t > 0 && mx < 0x7f800000u) atomicAdd(tiny + c, t);
       }
-      // the 16 threads of a half-warp share the plane row c
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-      if (tx == 0 && t > 0) atomicAdd(tiny + c, t);
     }
   }
 }
@@ -546,10 +546,11 @@ __global__ void __launch_bounds__(256) zero_split_tiles_kernel(const Gemm32Param
   int mt, nt;
   tile_coords(p, p.split_from + blockIdx.y, mt, nt);
   const int64_t r0 = (int64_t)mt * pair_bm, c0 = (int64_t)nt * BN;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < pair_bm * BN; idx += gridDim.x * blockDim.x) {
-    const int64_t r = r0 + idx / BN, c = c0 + idx % BN;
+  // one float4 of C per thread and step (ldc and n are multiples of 4)
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < pair_bm * BN / 4; idx += gridDim.x * blockDim.x) {
+    const int64_t r = r0 + idx / (BN / 4), c = c0 + 4 * (idx % (BN / 4));
     if (r < p.m && c < p.n) {
-      p.c[r * p.ldc + c] = 0.0f;
+      *reinterpret_cast<float4 *>(p.c + r * p.ldc + c) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (p.fixmap && (c & 31) == 0) p.fixmap[r * p.fix_words + (c >> 5)] = 0u;
     }
   }
@@ -926,22 +927,35 @@ __global__ void __launch_bounds__(256) gemm_f32_fixup_kernel(const float *__rest
                                                              int64_t lda, int64_t ldb, int64_t ldc, int bt,
                                                              int accumulate, const uint32_t *__restrict__ fixmap,
                                                              const uint32_t *__restrict__ fixrow, int64_t words) {
-  for (int64_t r = blockIdx.x; r < m; r += gridDim.x) {
-    if (fixrow[r] == 0) continue;
-    const uint32_t *map = fixmap + r * words;
-    const float *ar = a + r * lda;
-    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
-      if (!((map[j >> 5] >> (j & 31)) & 1u)) continue;
-      float sum = 0.0f;
-      if (bt) {
-        const float *bc = b + j * ldb;
-        for (int64_t q = 0; q < k; ++q) sum = fmaf(ar[q], bc[q], sum);
-      } else {
-        for (int64_t q = 0; q < k; ++q) sum = fmaf(ar[q], b[q * ldb + j], sum);
+  // CTA b owns rows b, b + grid, b + 2 grid, ...; it reads 256 of their flags
+  // at once (one load per thread) and works through the marked ones together.
+  __shared__ int64_t marked[256];
+  __shared__ int count;
+  const int64_t g = gridDim.x;
+  for (int64_t base = blockIdx.x; base < m; base += 256 * g) {
+    if (threadIdx.x == 0) count = 0;
+    __syncthreads();
+    const int64_t r = base + (int64_t)threadIdx.x * g;
+    if (r < m && fixrow[r]) marked[atomicAdd(&count, 1)] = r;
+    __syncthreads();
+    for (int q = 0; q < count; ++q) {
+      const int64_t row = marked[q];
+      const uint32_t *map = fixmap + row * words;
+      const float *ar = a + row * lda;
+      for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+        if (!((map[j >> 5] >> (j & 31)) & 1u)) continue;
+        float sum = 0.0f;
+        if (bt) {
+          const float *bc = b + j * ldb;
+          for (int64_t e = 0; e < k; ++e) sum = fmaf(ar[e], bc[e], sum);
+        } else {
+          for (int64_t e = 0; e < k; ++e) sum = fmaf(ar[e], b[e * ldb + j], sum);
+        }
+        float *cp = c + row * ldc + j;
+        *cp = accumulate ? *cp + sum : sum;
       }
-      float *cp = c + r * ldc + j;
-      *cp = accumulate ? *cp + sum : sum;
     }
+    __syncthreads();  // count and marked are rewritten for the next group
   }
 }
 
@@ -988,7 +1002,7 @@ ipuc_status launch_main(const CUtensorMap &tah, const CUtensorMap &tal, void *bh
     if (tail > 0 && 2 * tail <= pairs && chunks >= 2 && !(p.flags & IPUC_GEMM_ACCUMULATE)) {
       p.split_from = p.num_tiles - tail;
       p.num_units = p.num_tiles + tail;
-      zero_split_tiles_kernel<<<dim3(16, (unsigned)tail), 256, 0, stream>>>(p, PAIR_BM);
+      zero_split_tiles_kernel<<<dim3(64, (unsigned)tail), 256, 0, stream>>>(p, PAIR_BM);
       if ((st = check_launch("zero_split_tiles_kernel")) != IPUC_OK) return st;
     }
     IPUC_CUDA(cudaFuncSetAttribute(gemm_split3_pair_kernel<kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
