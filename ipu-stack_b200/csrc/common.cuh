@@ -40,7 +40,6 @@ enum : uint32_t {
   ERR_SITE_PRODUCER = 1,
   ERR_SITE_MMA = 2,
   ERR_SITE_EPILOGUE = 3,
-  ERR_SITE_SPLIT = 4,      // a K-split hand-off flag never arrived
   ERR_KERNEL_GEMM_F16 = 1u << 16,
   ERR_KERNEL_GEMM_F32 = 2u << 16,
   ERR_KERNEL_ATTENTION = 3u << 16,

@@ -20,8 +20,6 @@
 #include "sm100.cuh"
 #include "tma_host.cuh"
 
-#include <atomic>
-
 namespace ipuc {
 namespace {
 
@@ -45,41 +43,7 @@ struct GemmParams {
   int64_t num_tiles;
   uint32_t flags;
   uint32_t *err;
-  // CTA-pair kernel work units: units [0, split_from) are whole tiles; a
-  // last wave at most half full runs each of its tiles as two units, one
-  // per half of the k-blocks (see split_role).  No split: split_from =
-  // num_units = num_tiles.
-  int64_t num_units, split_from;
-  uint32_t epoch;  // this launch's tag in the split hand-off flags
 };
-
-// Split hand-off of a partial last wave: the first K half ("producer") of a
-// tile stores its partial sum into the tile's own C region (rounded to C's
-// precision, as the reference kernel rounds its f16 partials between K
-// blocks, gemm_f16_amp.S:363-437) and raises a flag; the second half
-// ("consumer") waits for the flag, adds the partial to its accumulator and
-// runs the normal epilogue (accumulate, GELU, rounding).  Both halves of a
-// tile run in the same wave of a persistent grid, so the wait is short.
-// Flags are tagged with a per-launch epoch and spread over kSplitSlots
-// launch slots, so launches that overlap on the GPU (other streams) use
-// different flags unless kSplitSlots launches apart are in flight at once.
-constexpr int kSplitSlots = 64, kSplitFlagsPerSlot = 256;
-__device__ uint32_t g_split_flags[kSplitSlots * kSplitFlagsPerSlot];
-
-struct SplitUnit {
-  int64_t tile;
-  int kb0, kb1;
-  int role;  // 0 whole tile, 1 producer (first K half), 2 consumer (second K half)
-};
-__device__ __forceinline__ SplitUnit split_role(const GemmParams &p, int64_t u) {
-  if (u < p.split_from) return {u, 0, p.k_blocks, 0};
-  const int64_t v = u - p.split_from;
-  const int mid = p.k_blocks / 2;
-  return {p.split_from + v / 2, (v & 1) ? mid : 0, (v & 1) ? p.k_blocks : mid, (v & 1) ? 2 : 1};
-}
-__device__ __forceinline__ uint32_t *split_flag(const GemmParams &p, int64_t tile, uint32_t rank) {
-  return g_split_flags + (p.epoch % kSplitSlots) * kSplitFlagsPerSlot + 2 * (tile - p.split_from) + rank;
-}
 
 __device__ __forceinline__ void tile_coords(const GemmParams &p, int64_t t, int &b, int &mt, int &nt) {
   const int64_t per = (int64_t)p.tiles_m * p.tiles_n;
@@ -163,88 +127,6 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int b, int64_t 
         cp[j] = (uint16_t)h;
       }
     }
-  }
-}
-
-// Split hand-off helpers (pair kernel).  The partial is C's element type:
-// f16 (rounded, no GELU) or f32.
-__device__ __forceinline__ void store_partial(const GemmParams &p, int b, int64_t row, int64_t col0,
-                                              const uint32_t (&r)[32], bool vec_ok, bool out_f32) {
-  const bool full_chunk = vec_ok && (col0 + 32 <= p.n);
-  if (out_f32) {
-    float *cp = static_cast<float *>(p.c) + b * p.stride_c + row * p.ldc + col0;
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        reinterpret_cast<uint4 *>(cp)[j] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
-    } else {
-      for (int j = 0; j < 32 && col0 + j < p.n; ++j) cp[j] = __uint_as_float(r[j]);
-    }
-  } else {
-    uint16_t *cp = static_cast<uint16_t *>(p.c) + b * p.stride_c + row * p.ldc + col0;
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        reinterpret_cast<uint4 *>(cp)[j] =
-            make_uint4(pack_h2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
-                       pack_h2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
-                       pack_h2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
-                       pack_h2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
-    } else {
-      for (int j = 0; j < 32 && col0 + j < p.n; ++j) cp[j] = f2h(__uint_as_float(r[j]));
-    }
-  }
-}
-
-// Adds the producer's partial (read from C, bypassing L1) into r.
-__device__ __forceinline__ void add_partial(const GemmParams &p, int b, int64_t row, int64_t col0, uint32_t (&r)[32],
-                                            bool vec_ok, bool out_f32) {
-  const bool full_chunk = vec_ok && (col0 + 32 <= p.n);
-  if (out_f32) {
-    const float *cp = static_cast<const float *>(p.c) + b * p.stride_c + row * p.ldc + col0;
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 o = __ldcg(reinterpret_cast<const float4 *>(cp) + j);
-        r[4 * j] = __float_as_uint(__uint_as_float(r[4 * j]) + o.x);
-        r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + o.y);
-        r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + o.z);
-        r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + o.w);
-      }
-    } else {
-      for (int j = 0; j < 32 && col0 + j < p.n; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __ldcg(cp + j));
-    }
-  } else {
-    const uint16_t *cp = static_cast<const uint16_t *>(p.c) + b * p.stride_c + row * p.ldc + col0;
-    if (full_chunk) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 o = __ldcg(reinterpret_cast<const uint4 *>(cp) + j);
-        const uint16_t *h = reinterpret_cast<const uint16_t *>(&o);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) r[8 * j + e] = __float_as_uint(__uint_as_float(r[8 * j + e]) + h2f(h[e]));
-      }
-    } else {
-      for (int j = 0; j < 32 && col0 + j < p.n; ++j)
-        r[j] = __float_as_uint(__uint_as_float(r[j]) + h2f(__ldcg(cp + j)));
-    }
-  }
-}
-
-__device__ __forceinline__ void split_signal(uint32_t *flag, uint32_t epoch) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
-}
-
-// Bounded wait (4 s, or until another role aborts) for the flag to carry epoch.
-__device__ __forceinline__ bool split_wait(const uint32_t *flag, uint32_t epoch, volatile int *abort) {
-  const uint64_t t0 = global_timer_ns();
-  for (;;) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if (v == epoch) return true;
-    if (*abort) return false;
-    if (global_timer_ns() - t0 > 4000000000ull) return false;
-    __nanosleep(256);
   }
 }
 
@@ -466,11 +348,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int64_t u = pair; u < p.num_units && ok; u += pairs) {
-        const SplitUnit w = split_role(p, u);
+      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs) {
         int b, mt, nt;
-        tile_coords(p, w.tile, b, mt, nt);  // mt counts 256-row pair tiles
-        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+        tile_coords(p, t, b, mt, nt);  // mt counts 256-row pair tiles
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % P_STAGES;
           const uint32_t ph = (it / P_STAGES) & 1u;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
@@ -508,8 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       bool ok = true;
       const uint64_t a_desc0 = make_smem_desc(smem_u32(smem), kAKMajor ? 16 : 8192, 1024, kSwizzle128B);
       const uint64_t b_desc0 = make_smem_desc(smem_u32(smem) + P_A_BYTES, kBKMajor ? 16 : 8192, 1024, kSwizzle128B);
-      for (int64_t u = pair; u < p.num_units && ok; u += pairs, ++local) {
-        const SplitUnit w = split_role(p, u);
+      for (int64_t t = pair; t < p.num_tiles && ok; t += pairs, ++local) {
         const uint32_t buf = local & 1u, use = local >> 1;
         if (!mbar_wait_bounded(&tmem_empty[buf], (use & 1u) ^ 1u, abort_flag)) {
           ok = false;
@@ -517,7 +397,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const int s = it % P_STAGES;
           const uint32_t ph = (it / P_STAGES) & 1u;
           if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
@@ -533,7 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t adesc = ad + (uint64_t)((kAKMajor ? k * 32 : k * 2048) >> 4);
             const uint64_t bdesc = bd + (uint64_t)((kBKMajor ? k * 32 : k * 2048) >> 4);
-            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
+            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           mma_commit_pair(&empty[s], 0x3);
         }
@@ -552,8 +432,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     const bool gelu = (p.flags & IPUC_GEMM_EPILOGUE_GELU) != 0;
     const bool vec_ok = (p.ldc % 8 == 0) && (p.stride_c % 8 == 0) && (p.ld_add % 8 == 0) && (p.stride_add % 8 == 0);
     uint32_t local = 0;
-    for (int64_t u = pair; u < p.num_units; u += pairs, ++local) {
-      const SplitUnit w = split_role(p, u);
+    for (int64_t t = pair; t < p.num_tiles; t += pairs, ++local) {
       const uint32_t buf = local & 1u, use = local >> 1;
       if (!mbar_wait_bounded(&tmem_full[buf], use & 1u, abort_flag)) {
         record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_EPILOGUE);
@@ -562,39 +441,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       }
       tc_fence_after();
       int b, mt, nt;
-      tile_coords(p, w.tile, b, mt, nt);
+      tile_coords(p, t, b, mt, nt);
       const int64_t row = (int64_t)mt * PAIR_BM + (int64_t)rank * BM + quarter * 32 + lane;
       const bool row_ok = row < p.m;
-      if (w.role == 2) {
-        // wait for the first K half's partial sum of these 128 rows
-        if (threadIdx.x == 64 && !split_wait(split_flag(p, w.tile, rank), p.epoch, abort_flag)) {
-          record_device_error(p.err, ERR_KERNEL_GEMM_F16 | ERR_SITE_SPLIT);
-          *abort_flag = 1;
-        }
-        named_barrier_sync(1, 128);
-      }
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + buf * BN + chunk * 32 + ((uint32_t)(quarter * 32) << 16), r);
         tmem_wait_ld(r);
         const int64_t col0 = (int64_t)nt * BN + chunk * 32;
         if (!row_ok || col0 >= p.n) continue;
-        if (w.role == 1) {
-          store_partial(p, b, row, col0, r, vec_ok, out_f32);
-          continue;
-        }
-        if (w.role == 2) add_partial(p, b, row, col0, r, vec_ok, out_f32);
         store_chunk(p, b, row, col0, r, vec_ok, out_f32, accumulate, gelu);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(&tmem_empty[buf]);
-      if (w.role == 1) {
-        // publish this CTA's partial: every thread's stores, then the flag
-        __threadfence();
-        named_barrier_sync(1, 128);
-        if (threadIdx.x == 64) split_signal(split_flag(p, w.tile, rank), p.epoch);
-      }
     }
   }
   tc_fence_before();
@@ -783,7 +643,6 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
   p.k_blocks = (int32_t)((k + BK - 1) / BK);
   p.flags = flags;
   p.err = device_error_word();
-  p.epoch = 0;
   const int sms = sm_count();
   // Small problems (at most a quarter wave of 128 x 256 tiles): the latency
   // form, 128 x 64 tiles, one per CTA, with programmatic dependent launch.
@@ -796,7 +655,6 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
     p.tiles_m = (int32_t)((m + BM - 1) / BM);
     p.tiles_n = (int32_t)((n + SBN - 1) / SBN);
     p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
-    p.split_from = p.num_units = p.num_tiles;
     auto go = [&](auto kernel) -> ipuc_status {
       IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM_BYTES));
       cudaLaunchConfig_t cfg = {};
@@ -827,22 +685,6 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
     if (bt) st = make_map_3d(&tbp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, k, n, batch, ldb, batch > 1 ? sb : 0, BK, PB_N);
     else st = make_map_3d(&tbp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, n, k, batch, ldb, batch > 1 ? sb : 0, 64, BK);
     if (st != IPUC_OK) return st;
-    // A last wave at most half full runs as two K halves per tile (two units
-    // each, on different pairs of the same wave), so that it takes about
-    // half a wave-time.  Not when C is itself the accumulation source (the
-    // hand-off goes through C).
-    const int64_t tail = p.num_tiles % pairs;
-    p.split_from = p.num_units = p.num_tiles;
-    const bool c_is_source = (flags & IPUC_GEMM_ACCUMULATE) && p.add == c;
-    if (tail > 0 && 2 * tail <= pairs && p.k_blocks >= 8 && !c_is_source &&
-        2 * tail <= kSplitFlagsPerSlot) {
-      static std::atomic<uint32_t> epochs{0};
-      uint32_t e = epochs.fetch_add(1) + 1;
-      if (e == 0) e = epochs.fetch_add(1) + 1;  // 0 is the flags' initial value
-      p.epoch = e;
-      p.split_from = p.num_tiles - tail;
-      p.num_units = p.num_tiles + tail;
-    }
     auto go = [&](auto kernel) -> ipuc_status {
       IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
       kernel<<<(unsigned)(2 * pairs), 192, P_SMEM_BYTES, stream>>>(tap, tbp, p);
@@ -853,7 +695,6 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
   }
   p.tiles_m = (int32_t)((m + BM - 1) / BM);
   p.num_tiles = (int64_t)p.tiles_m * p.tiles_n * batch;
-  p.split_from = p.num_units = p.num_tiles;
   const int grid = (int)(p.num_tiles < sms ? p.num_tiles : sms);
   auto go = [&](auto kernel) -> ipuc_status {
     IPUC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));

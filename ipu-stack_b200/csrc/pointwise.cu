@@ -221,6 +221,47 @@ extern "C" ipuc_status ipuc_add_f16(void *out, const void *left, const void *rig
   return check_launch("add_f16_kernel");
 }
 
+// f16 -> f32 over whole 4096-element tiles (8 KB in, 16 KB out): each
+// thread converts 16 elements into a shared staging tile and one thread
+// writes the tile out as a single 16 KB bulk copy (cp.async.bulk), two
+// staging tiles in rotation.  The output is twice the input, and long
+// contiguous bulk writes keep the DRAM write stream efficient.
+constexpr int CAST_TILE = 4096;
+__global__ void __launch_bounds__(256) cast_f16_f32_bulk_kernel(float *__restrict__ out,
+                                                                const uint16_t *__restrict__ in, int64_t tiles) {
+  __shared__ __align__(128) float stage[2][CAST_TILE];
+  int buf = 0;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, buf ^= 1) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(in + t * CAST_TILE) + 2 * threadIdx.x;
+    const uint4 x0 = __ldcs(src), x1 = __ldcs(src + 1);
+    if (threadIdx.x == 0) {
+      // the staging tile written two tiles ago has been read out by its copy
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    }
+    __syncthreads();
+    float4 *dst = reinterpret_cast<float4 *>(stage[buf]) + 4 * threadIdx.x;
+    const __half2 *h0 = reinterpret_cast<const __half2 *>(&x0), *h1 = reinterpret_cast<const __half2 *>(&x1);
+    float2 f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[i] = __half22float2(h0[i]);
+      f[4 + i] = __half22float2(h1[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_float4(f[2 * i].x, f[2 * i].y, f[2 * i + 1].x, f[2 * i + 1].y);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t sa = (uint32_t)__cvta_generic_to_shared(stage[buf]);
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(out + t * CAST_TILE), "r"(sa),
+                   "r"((uint32_t)(CAST_TILE * 4))
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+  if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 extern "C" ipuc_status ipuc_cast(void *out, ipuc_precision to, const void *in, ipuc_precision from,
                                  uint64_t element_count, ipuc_stream stream) {
   IPUC_CHECK_ARG((to == IPUC_F16 || to == IPUC_F32) && (from == IPUC_F16 || from == IPUC_F32), "cast: bad precision");
@@ -228,15 +269,31 @@ extern "C" ipuc_status ipuc_cast(void *out, ipuc_precision to, const void *in, i
   IPUC_CHECK_ARG(out && in, "cast: null pointer");
   const int64_t n = (int64_t)element_count;
   if (to != from && aligned(out, 16) && aligned(in, 16) && n >= 8) {
-    const int64_t chunks = n / 8, done = chunks * 8;
+    const int64_t tiles = to == IPUC_F32 ? n / CAST_TILE : 0;
+    if (tiles > 0) {
+      const int64_t cap = (int64_t)sm_count() * 6;
+      cast_f16_f32_bulk_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(
+          static_cast<float *>(out), static_cast<const uint16_t *>(in), tiles);
+      const ipuc_status st = check_launch("cast_f16_f32_bulk_kernel");
+      if (st != IPUC_OK) return st;
+      if (tiles * CAST_TILE == n) return IPUC_OK;
+      out = static_cast<float *>(out) + tiles * CAST_TILE;
+      in = static_cast<const uint16_t *>(in) + tiles * CAST_TILE;
+    }
+    const int64_t rest = n - tiles * CAST_TILE;
+    const int64_t chunks = rest / 8, done = chunks * 8;
+    if (chunks == 0) {
+      cast_kernel<<<1, 256, 0, stream>>>(out, to, in, from, rest);
+      return check_launch("cast_kernel");
+    }
     if (to == IPUC_F32)
       cast_vec_kernel<true><<<grid_for(chunks, 256), 256, 0, stream>>>(out, in, chunks);
     else
       cast_vec_kernel<false><<<grid_for(chunks, 256), 256, 0, stream>>>(out, in, chunks);
-    if (done < n) {
+    if (done < rest) {
       const size_t ob = to == IPUC_F16 ? 2 : 4, ib = from == IPUC_F16 ? 2 : 4;
       cast_kernel<<<1, 256, 0, stream>>>(static_cast<uint8_t *>(out) + done * ob, to,
-                                         static_cast<const uint8_t *>(in) + done * ib, from, n - done);
+                                         static_cast<const uint8_t *>(in) + done * ib, from, rest - done);
     }
     return check_launch("cast_vec_kernel");
   }

@@ -183,18 +183,17 @@ def test_gemm_a_transposed_batched_gelu():
 
 @pytest.mark.parametrize("flags,with_c", [(0, False), (ipuc.GEMM_EPILOGUE_GELU, False), (ipuc.GEMM_OUT_F32, False),
                                           (ipuc.GEMM_ACCUMULATE, True), (ipuc.GEMM_B_TRANSPOSED, False)])
-def test_gemm_split_tail_wave(flags, with_c):
-    """80 pair tiles (2048 x 2560) on the CTA-pair kernel: the last, partial
-    wave runs each tile as two K halves that hand off through C (not when C is
-    the accumulation source)."""
+def test_gemm_partial_last_wave(flags, with_c):
+    """80 pair tiles (2048 x 2560) on the persistent CTA-pair kernel: a full
+    wave of 74 pair slots and a partial one, with every epilogue."""
     got, ref = run_case(2048, 2560, 1024, flags, seed=77 + flags, with_c=with_c)
     ok, msg = f16_close(got, ref)
     assert ok, msg
 
 
-def test_gemm_split_tail_with_addend():
-    """gemm_f16_addend (C = A.B + D, D separate) with the split tail, twice in a
-    row (the hand-off flags are tagged per launch)."""
+def test_gemm_partial_last_wave_with_addend():
+    """gemm_f16_addend (C = A.B + D, D separate) on the same shape, twice in a
+    row."""
     m, n, k = 2048, 2560, 1024
     a = oracle.f16_bits(seeded_normal(91, (m, k), 0.1))
     b = oracle.f16_bits(seeded_normal(92, (k, n), 0.1))

@@ -65,10 +65,10 @@ def test_add_f16(n, lp, rp):
     assert np.array_equal(host_u16(out), want)
 
 
-@pytest.mark.parametrize("n", [5000, 5003, 7, 1 << 20])
+@pytest.mark.parametrize("n", [5000, 5003, 7, 4100, 3 * 4096 + 8, 1 << 20])
 def test_cast_round_trip(n):
-    """Bit-exact both ways: the 8-element vector path, its scalar tail and
-    short inputs."""
+    """Bit-exact both ways: whole 4096-element tiles (f16 -> f32 bulk-store
+    kernel), the 8-element vector path, its scalar tail and short inputs."""
     x = seeded_normal(3, n, 100.0)
     xd = dev_f32(x)
     h = empty_u16(n)
