@@ -997,6 +997,19 @@ def profile_case(kernel: str):
             y16.normal_()
             g16 = torch.empty_like(y16)
             run = lambda: ipuc.call("ipuc_gelu_f16", g16.data_ptr(), y16.data_ptr(), cnt, s)
+    elif kernel == "cast":
+        # config 5's activation (8192 x 4096) f16 -> f32
+        na = 8192 * 4096
+        x16 = torch.randn(na, device="cuda").half()
+        x32 = torch.empty(na, device="cuda")
+        run = lambda: ipuc.call("ipuc_cast", x32.data_ptr(), ipuc.F32, x16.data_ptr(), ipuc.F16, na, s)
+    elif kernel == "gemm_small":
+        # config 1: 256^3 FP16 GEMM (the latency kernel)
+        m = n = k = 256
+        a = (torch.randn((m, k), device="cuda") * 0.1).half()
+        b = (torch.randn((k, n), device="cuda") * 0.1).half()
+        c = torch.empty((m, n), device="cuda", dtype=torch.float16)
+        run = lambda: ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, 0, s)
     else:
         m = n = k = 4096
         a = torch.rand((m, k), device="cuda")
@@ -1024,7 +1037,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=30.0,
                     help="CPU baseline budget: three all-core legs of a third each, plus a 1-core leg")
     ap.add_argument("--profile", choices=["gemm", "attention", "attention8", "rearrange", "rearrange_amp_left",
-                                          "gemm_f32", "reduce", "gelu"],
+                                          "gemm_f32", "reduce", "gelu", "cast", "gemm_small"],
                     help="run a few launches of one kernel on a small case (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile:

@@ -918,19 +918,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 inline uint64_t round256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
 // Recomputes the C elements the 3xF16 epilogue marked (tiny or non-finite
-// operands, see above) as plain fp32 FMA dot products over k, in k order:
-// C = (IPUC_GEMM_ACCUMULATE ? C : 0) + sum_k A[r][k] B[k][j].  One CTA per row
-// with a marked element (grid-stride over the rows; unmarked rows cost one
-// load), threads over the row's columns.
+// operands, see above) as fp32 FMA dot products: C = (IPUC_GEMM_ACCUMULATE ?
+// C : 0) + sum_k A[r][k] B[k][j].  One warp per marked element: lane l sums
+// k = l, l + 32, ... (32 loads in flight instead of a k-long chain of
+// dependent ones), then the lanes' sums are added in a fixed butterfly order.
+// CTA b owns rows b, b + grid, b + 2 grid, ...; it reads 256 of their flags at
+// once (one load per thread) and its 8 warps share the marked rows' words.
 __global__ void __launch_bounds__(256) gemm_f32_fixup_kernel(const float *__restrict__ a, const float *__restrict__ b,
                                                              float *__restrict__ c, int64_t m, int64_t n, int64_t k,
                                                              int64_t lda, int64_t ldb, int64_t ldc, int bt,
                                                              int accumulate, const uint32_t *__restrict__ fixmap,
                                                              const uint32_t *__restrict__ fixrow, int64_t words) {
-  // CTA b owns rows b, b + grid, b + 2 grid, ...; it reads 256 of their flags
-  // at once (one load per thread) and works through the marked ones together.
   __shared__ int64_t marked[256];
   __shared__ int count;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t g = gridDim.x;
   for (int64_t base = blockIdx.x; base < m; base += 256 * g) {
     if (threadIdx.x == 0) count = 0;
@@ -942,17 +943,29 @@ __global__ void __launch_bounds__(256) gemm_f32_fixup_kernel(const float *__rest
       const int64_t row = marked[q];
       const uint32_t *map = fixmap + row * words;
       const float *ar = a + row * lda;
-      for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
-        if (!((map[j >> 5] >> (j & 31)) & 1u)) continue;
-        float sum = 0.0f;
-        if (bt) {
-          const float *bc = b + j * ldb;
-          for (int64_t e = 0; e < k; ++e) sum = fmaf(ar[e], bc[e], sum);
-        } else {
-          for (int64_t e = 0; e < k; ++e) sum = fmaf(ar[e], b[e * ldb + j], sum);
+      for (int64_t wd = warp; wd < words; wd += 8) {
+        uint32_t bits = map[wd];
+        while (bits) {
+          const int bit = __ffs(bits) - 1;
+          bits &= bits - 1;
+          const int64_t j = wd * 32 + bit;
+          if (j >= n) break;
+          float sum = 0.0f;
+          if (bt) {
+            const float *bc = b + j * ldb;
+#pragma unroll 4
+            for (int64_t e = lane; e < k; e += 32) sum = fmaf(ar[e], bc[e], sum);
+          } else {
+#pragma unroll 4
+            for (int64_t e = lane; e < k; e += 32) sum = fmaf(ar[e], b[e * ldb + j], sum);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          if (lane == 0) {
+            float *cp = c + row * ldc + j;
+            *cp = accumulate ? *cp + sum : sum;
+          }
         }
-        float *cp = c + row * ldc + j;
-        *cp = accumulate ? *cp + sum : sum;
       }
     }
     __syncthreads();  // count and marked are rewritten for the next group
