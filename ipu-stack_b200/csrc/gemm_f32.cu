@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(256) split_f16_rows_kernel(const float *__rest
 // floats keeps the column reads conflict-free); pad elements [rows, ldp) of
 // each plane row are zero.  Full 64x64 tiles need rows, cols and ld multiples
 // of 4 (the gemm_f32 entry requires that); ragged tiles use scalar loads.
-__global__ void __launch_bounds__(256) split_f16_transpose_kernel(const float *__restrict__ src, int64_t rows,
+__global__ void __launch_bounds__(256, 8) split_f16_transpose_kernel(const float *__restrict__ src, int64_t rows,
                                                                   int64_t cols, int64_t ld,
                                                                   const uint32_t *__restrict__ cmax, int64_t ldp,
                                                                   __half *__restrict__ hi, __half *__restrict__ lo,
