@@ -155,3 +155,16 @@ def test_shards_reproduce_unsharded_evaluation_gloo(case, world, reduces):
     for rank, ok, msg, n in res:
         assert ok, f"rank {rank}: {msg}"
         assert n == reduces
+
+
+def test_sharded_session_arguments_checked_before_any_device_work():
+    import ipuc
+    from ipuc.graph import Session
+    g, *_ = block(2, 64, 256, 4, 512)
+    with pytest.raises(ipuc.IpucError) as e:
+        Session(g, rank=0, world=2)            # no NCCL unique id
+    assert e.value.status == ipuc.ERR_INVALID_ARGUMENT and "unique id" in str(e.value)
+    with pytest.raises(ValueError, match="rank must lie"):
+        g.plan(2, 2)                            # rank outside [0, world)
+    with pytest.raises(ValueError, match="rank must lie"):
+        g.shard(0, 0)
