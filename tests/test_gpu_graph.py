@@ -1,6 +1,8 @@
 """ComputeGraph -> per-GPU lowering -> session, checked end to end against the
 oracle's restatement of the host evaluator (diagnostic.rs:411-847), with the
 FP16 tolerance max|err| <= 2e-2*max|ref|, rel-L2 <= 5e-3."""
+import os
+
 import numpy as np
 import pytest
 
@@ -233,3 +235,67 @@ def test_per_op_diagnostic_walks_every_value():
     avail = {r["value"]: r["available"] for r in fused.diagnose({v: ref[v] for v in op_values})}
     assert avail[out] and not all(avail.values())
     fused.close()
+
+
+def _reference_check(got, ref, atol=0.03, rtol=0.05):
+    """The hardware tests' acceptance rule for these workloads:
+    |got - ref| <= 0.03 + 0.05 |ref| element by element."""
+    err = np.abs(got.astype(np.float64) - ref)
+    return bool((err <= atol + rtol * np.abs(ref)).all()), float(err.max())
+
+
+def test_siglip_mlp_benchmark_shape():
+    """The siglip-mlp-benchmark graph shape (B=4, T=729, D=1152,
+    H=4304; two blocks, so the reference builds it as a Repeat over value
+    sequences of [1, D, H] / [1, H, D] weights), seeded N(0, 1) inputs and
+    N(0, 1/D) / N(0, 1/H) weights, against the evaluator: the hardware test's
+    rule and the FP16 tolerance."""
+    B, T, D, H, blocks = 4, 729, 1152, 4304, 2
+    g = ComputeGraph()
+    x = g.host_input("left", [B, T, D])
+    ups = [g.parameter(f"up{i}", [1, D, H]) for i in range(blocks)]
+    downs = [g.parameter(f"down{i}", [1, H, D]) for i in range(blocks)]
+    su, sd = g.value_sequence("MLP up weights", ups), g.value_sequence("MLP down weights", downs)
+    y = g.repeat(blocks, [x], [], [su, sd],
+                 lambda b, a: [b.gemm(b.gelu(b.gemm(a.carried[0], a.iterated[0])), a.iterated[1])])[0]
+    g.set_outputs([y])
+    rng = np.random.default_rng(729)
+    inputs = {x: rng.standard_normal((B, T, D)).astype(np.float32)}
+    for v in ups:
+        inputs[v] = (rng.standard_normal((1, D, H)) / np.sqrt(D)).astype(np.float32)
+    for v in downs:
+        inputs[v] = (rng.standard_normal((1, H, D)) / np.sqrt(H)).astype(np.float32)
+    s = run_graph(g, inputs)
+    got = s.read(y).astype(np.float32)
+    ref = oracle.evaluate(g, inputs, threads=os.cpu_count() or 8)[y]
+    ok, worst = _reference_check(got, ref)
+    assert ok, worst
+    ok, msg = f16_close(got, ref)
+    assert ok, msg
+
+
+def test_siglip_attention_benchmark_shape():
+    """The siglip-attention-benchmark graph (16 heads of 72, 729 tokens: QKV
+    projections, SplitHeads, FlashAttention as the output), head_dim 72 padded
+    to the tensor-core tile inside the kernel."""
+    heads, tokens, hd = 16, 729, 72
+    width = heads * hd
+    g = ComputeGraph()
+    x = g.host_input("input", [1, tokens, width])
+    ws = {n: g.parameter(n, [width, width]) for n in ("query.weight", "key.weight", "value.weight")}
+    q, k, v = (g.split_heads(g.gemm(x, ws[n]), heads) for n in ("query.weight", "key.weight", "value.weight"))
+    out = g.flash_attention(q, k, v)
+    g.set_outputs([out])
+    rng = np.random.default_rng(72)
+    inputs = {x: rng.standard_normal((1, tokens, width)).astype(np.float32)}
+    for val in ws.values():
+        inputs[val] = (rng.standard_normal((width, width)) / np.sqrt(width)).astype(np.float32)
+    s = run_graph(g, inputs)
+    assert s.plan.count("split_heads_f16") == 3 and "flash_attention_f16" in s.plan
+    got = s.read(out).astype(np.float32)
+    ref = oracle.evaluate(g, inputs, threads=os.cpu_count() or 8)[out]
+    assert got.shape == (heads, tokens, hd)
+    ok, worst = _reference_check(got, ref)
+    assert ok, worst
+    ok, msg = f16_close(got, ref)
+    assert ok, msg
