@@ -38,7 +38,6 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
-#include <map>
 #include <memory>
 #include <mutex>
 #include <sstream>
@@ -67,7 +66,9 @@ struct RepeatInfo {
 };
 
 struct Op {
-  OpKind kind;
+  Op() = default;
+  Op(OpKind k, std::vector<int32_t> in, std::vector<int32_t> res) : kind(k), inputs(std::move(in)), results(std::move(res)) {}
+  OpKind kind = OpKind::Gemm;
   std::vector<int32_t> inputs;
   std::vector<int32_t> results;
   int32_t id = -1;  // operation id in construction order (body operations included)
@@ -674,8 +675,8 @@ ipuc_status lower(const FlatGraph &g, int rank, int world, bool fuse, Lowered &o
     }
     st.n = n;
     st.k = k;
-    st.flags |= op.transpose_right ? IPUC_GEMM_B_TRANSPOSED : 0u;
-    st.flags |= op.transpose_left ? IPUC_GEMM_A_TRANSPOSED : 0u;
+    st.flags |= op.transpose_right ? (uint32_t)IPUC_GEMM_B_TRANSPOSED : 0u;
+    st.flags |= op.transpose_left ? (uint32_t)IPUC_GEMM_A_TRANSPOSED : 0u;
     st.in0 = op.inputs[0];
     st.in1 = op.inputs[1];
     st.flop = 2.0 * (double)st.batch * (double)st.m * (double)n * (double)k;
