@@ -251,8 +251,9 @@ ipuc_status launch(const ipuc_kernel_spec &spec, const ipuc_tensor &out, const i
       const int64_t kb = g.b_transposed ? B.dims[rank - 1] : B.dims[rank - 2];
       if (kb != k || out.dims[rank - 2] != m || out.dims[rank - 1] != n)
         return fail(IPUC_ERR_INVALID_ARGUMENT, "gemm: operand shapes do not chain");
-      uint32_t flags = (g.mode == 1 ? IPUC_GEMM_ACCUMULATE : 0u) | (g.b_transposed ? IPUC_GEMM_B_TRANSPOSED : 0u) |
-                       (g.epilogue_gelu ? IPUC_GEMM_EPILOGUE_GELU : 0u);
+      uint32_t flags = (g.mode == 1 ? (uint32_t)IPUC_GEMM_ACCUMULATE : 0u) |
+                       (g.b_transposed ? (uint32_t)IPUC_GEMM_B_TRANSPOSED : 0u) |
+                       (g.epilogue_gelu ? (uint32_t)IPUC_GEMM_EPILOGUE_GELU : 0u);
       const int64_t ldb = g.b_transposed ? k : n;
       if (g.multiply == IPUC_F16) {
         if (out.precision == IPUC_F32) flags |= IPUC_GEMM_OUT_F32;
