@@ -299,3 +299,20 @@ def test_siglip_attention_benchmark_shape():
     assert ok, worst
     ok, msg = f16_close(got, ref)
     assert ok, msg
+
+
+@pytest.mark.parametrize("tr", [False, True])
+def test_transpose_left_batched_gemm(tr):
+    """transpose_left on a batched left operand [b, k, m] against a shared 2-D
+    right operand (batched GEMM with a zero right stride), with and without
+    transpose_right."""
+    g = ComputeGraph()
+    a = g.host_input("a", [3, 128, 192])           # [batch, k, m]
+    b = g.parameter("b", [256, 128] if tr else [128, 256])
+    c = g.gemm_with_options(a, b, transpose_left=True, transpose_right=tr)
+    g.set_outputs([c])
+    assert g.value_shape(c) == (3, 192, 256)
+    inputs = {a: seeded_normal(51, (3, 128, 192)), b: seeded_normal(52, (256, 128) if tr else (128, 256), 0.1)}
+    s = run_graph(g, inputs)
+    ok, msg = f16_close(s.read(c).astype(np.float32), oracle.evaluate(g, inputs)[c])
+    assert ok, msg
