@@ -122,7 +122,9 @@ ipuc_status ipuc_gemm_f16_addend(void *c, const void *a, const void *b, int64_t 
                                  int64_t ld_addend, ipuc_stream stream);
 
 /* Batched form: `batch` independent GEMMs at the given element strides
- * (batched-gemm-smoke, crates/ipu-tests/src/main.rs:201-220). */
+ * (batched-gemm-smoke, crates/ipu-tests/src/main.rs:201-220).  A stride of 0
+ * for A or B shares that operand across the batch (numpy broadcasting of a
+ * batch dimension); C's stride must be nonzero. */
 ipuc_status ipuc_gemm_f16_batched(void *c, const void *a, const void *b, int64_t batch,
                                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
                                   int64_t ldc, int64_t stride_a, int64_t stride_b,

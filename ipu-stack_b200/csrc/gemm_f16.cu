@@ -619,6 +619,25 @@ ipuc_status launch_gemm_f16(void *c, const void *a, const void *b, int64_t batch
                    "(16-byte TMA rows)");
   IPUC_CHECK_ALIGN(batch == 1 || (sa % 8 == 0 && sb % 8 == 0), "gemm_f16: batch strides must be multiples of 8");
   IPUC_CHECK_ARG(m < (1ll << 31) && n < (1ll << 31) && k < (1ll << 31) && batch < (1ll << 31), "gemm_f16: extent too large");
+  if (batch > 1 && (sa == 0 || sb == 0 || sc == 0)) {
+    // An operand shared by every batch entry (stride 0): a tensor map cannot
+    // repeat a tensor with stride 0.  With K-major A rows, B shared and the
+    // batches of A and C back to back, the batch is just more rows of one GEMM;
+    // otherwise each entry runs as its own GEMM.
+    IPUC_CHECK_ARG(sc != 0, "gemm_f16: batched C needs a nonzero stride");
+    const bool add_batched = addend == nullptr;  // the C-accumulate source follows C's stride
+    if (sb == 0 && sa != 0 && !at && sa == m * lda && sc == m * ldc && add_batched)
+      return launch_gemm_f16(c, a, b, 1, m * batch, n, k, lda, ldb, ldc, 0, 0, 0, flags, stream);
+    const size_t esz = (flags & IPUC_GEMM_OUT_F32) ? 4 : 2;
+    for (int64_t i = 0; i < batch; ++i) {
+      const ipuc_status st = launch_gemm_f16(static_cast<uint8_t *>(c) + i * sc * esz,
+                                             static_cast<const uint16_t *>(a) + i * sa,
+                                             static_cast<const uint16_t *>(b) + i * sb, 1, m, n, k, lda, ldb, ldc, 0,
+                                             0, 0, flags, stream, addend, ld_add);
+      if (st != IPUC_OK) return st;
+    }
+    return IPUC_OK;
+  }
   CUtensorMap ta, tb;
   // A: K-major [m x k] tiles of 128 x 64, or with IPUC_GEMM_A_TRANSPOSED
   // M-major ([k x m] rows, 64-row boxes of 64 k).

@@ -205,3 +205,26 @@ def test_gemm_partial_last_wave_with_addend():
         ok, msg = f16_close(f16_of(host_u16(c)).reshape(m, n), ref)
         assert ok, msg
     ipuc.device_status()
+
+
+@pytest.mark.parametrize("shared", ["a", "b"])
+@pytest.mark.parametrize("at", [False, True])
+def test_gemm_batched_shared_operand(shared, at):
+    """ipuc_gemm_f16_batched with a zero stride: one operand shared by every
+    batch entry (K-major A with shared B takes the one-GEMM path; the others
+    run per entry)."""
+    batch, m, n, k = 3, 256, 192, 128
+    a_shape = (k, m) if at else (m, k)
+    a = oracle.f16_bits(seeded_normal(61, (1 if shared == "a" else batch,) + a_shape, 0.1))
+    b = oracle.f16_bits(seeded_normal(62, (1 if shared == "b" else batch, k, n), 0.1))
+    af = np.broadcast_to(f16_of(a), (batch,) + a_shape)
+    bf = np.broadcast_to(f16_of(b), (batch, k, n))
+    ref = oracle.quantize_f16(oracle.gemm(af, bf, at, False))
+    c = empty_u16(batch * m * n)
+    flags = ipuc.GEMM_A_TRANSPOSED if at else 0
+    ad, bd = dev_u16(a), dev_u16(b)
+    ipuc.call("ipuc_gemm_f16_batched", c.data_ptr(), ad.data_ptr(), bd.data_ptr(), batch, m, n, k,
+              m if at else k, n, n, 0 if shared == "a" else m * k, 0 if shared == "b" else k * n, m * n, flags,
+              torch.cuda.current_stream().cuda_stream)
+    ok, msg = f16_close(f16_of(host_u16(c)).reshape(batch, m, n), ref)
+    assert ok, msg
