@@ -955,11 +955,50 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def attention_vendor_compare():
+    """Config 4 through this library's attention and through torch's SDPA on its
+    cuDNN backend (the vendor's sm100 attention), alternating 10-launch batches
+    timed by CUDA events: a measured reference point for what the hardware
+    sustains on this shape, printed as TFLOP/s per batch."""
+    import torch
+    import ipuc
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    torch.cuda.set_device(0)
+    s = torch.cuda.current_stream().cuda_stream
+    B, H, S, D = ATT_B, ATT_H, ATT_S, ATT_D
+    q, k, v = (torch.randn((B, H, S, D), device="cuda").half() for _ in range(3))
+    o = torch.empty_like(q)
+    flop = 4.0 * B * H * S * S * D
+    ours = lambda: ipuc.call("ipuc_flash_attention_f16", o.data_ptr(), ipuc.F16, q.data_ptr(), k.data_ptr(),
+                             v.data_ptr(), B * H, S, S, D, 0.0, s)
+
+    def vendor():
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            torch.nn.functional.scaled_dot_product_attention(q, k, v)
+
+    rates = {"ipuc": [], "cudnn": []}
+    for _ in range(3):
+        ours(), vendor()
+    for _ in range(4):
+        for name, fn in (("ipuc", ours), ("cudnn", vendor)):
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record()
+            for _ in range(10):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            rates[name].append(round(flop * 10 / (a.elapsed_time(b) * 1e-3) / 1e12, 1))
+    print(json.dumps({"case": "attention_vendor", "tflops": rates}))
+
+
 def profile_case(kernel: str):
     """One kernel at the exact shape the headline step launches it with (at most
     ~1.3 GB on the device), for ncu captures: 1 warm-up + 3 launches."""
     import torch
     import ipuc
+    if kernel == "attention_vendor":
+        attention_vendor_compare()
+        return
     torch.cuda.set_device(0)
     s = torch.cuda.current_stream().cuda_stream
     if kernel == "gemm":
@@ -1037,7 +1076,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=30.0,
                     help="CPU baseline budget: three all-core legs of a third each, plus a 1-core leg")
     ap.add_argument("--profile", choices=["gemm", "attention", "attention8", "rearrange", "rearrange_amp_left",
-                                          "gemm_f32", "reduce", "gelu", "cast", "gemm_small"],
+                                          "gemm_f32", "reduce", "gelu", "cast", "gemm_small", "attention_vendor"],
                     help="run a few launches of one kernel on a small case (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile:
