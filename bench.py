@@ -991,6 +991,41 @@ def attention_vendor_compare():
     print(json.dumps({"case": "attention_vendor", "tflops": rates}))
 
 
+def gemm_vendor_compare():
+    """Config 3's GEMM (8192x4096 . 4096x16384, f16) through this library (GELU
+    fused, and without the epilogue) and through torch.matmul (cuBLAS, no GELU),
+    alternating 10-launch batches timed by CUDA events, TFLOP/s per batch."""
+    import torch
+    import ipuc
+    torch.cuda.set_device(0)
+    s = torch.cuda.current_stream().cuda_stream
+    m, n, k = MLP_M, MLP_N, MLP_K
+    a = torch.randn((m, k), device="cuda").half()
+    b = (torch.randn((k, n), device="cuda") / 64).half()
+    c = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    flop = 2.0 * m * n * k
+    fns = {
+        "ipuc_gelu": lambda: ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n,
+                                       ipuc.GEMM_EPILOGUE_GELU, s),
+        "ipuc": lambda: ipuc.call("ipuc_gemm_f16", c.data_ptr(), a.data_ptr(), b.data_ptr(), m, n, k, k, n, n, 0, s),
+        "cublas": lambda: torch.matmul(a, b, out=c),
+    }
+    rates = {name: [] for name in fns}
+    for fn in fns.values():
+        for _ in range(3):
+            fn()
+    for _ in range(4):
+        for name, fn in fns.items():
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            for _ in range(10):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            rates[name].append(round(flop * 10 / (e0.elapsed_time(e1) * 1e-3) / 1e12, 1))
+    print(json.dumps({"case": "gemm_vendor", "tflops": rates}))
+
+
 def profile_case(kernel: str):
     """One kernel at the exact shape the headline step launches it with (at most
     ~1.3 GB on the device), for ncu captures: 1 warm-up + 3 launches."""
@@ -998,6 +1033,9 @@ def profile_case(kernel: str):
     import ipuc
     if kernel == "attention_vendor":
         attention_vendor_compare()
+        return
+    if kernel == "gemm_vendor":
+        gemm_vendor_compare()
         return
     torch.cuda.set_device(0)
     s = torch.cuda.current_stream().cuda_stream
@@ -1076,7 +1114,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=30.0,
                     help="CPU baseline budget: three all-core legs of a third each, plus a 1-core leg")
     ap.add_argument("--profile", choices=["gemm", "attention", "attention8", "rearrange", "rearrange_amp_left",
-                                          "gemm_f32", "reduce", "gelu", "cast", "gemm_small", "attention_vendor"],
+                                          "gemm_f32", "reduce", "gelu", "cast", "gemm_small", "attention_vendor",
+                                          "gemm_vendor"],
                     help="run a few launches of one kernel on a small case (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile:
