@@ -245,7 +245,7 @@ def _reference_check(got, ref, atol=0.03, rtol=0.05):
 
 
 def test_siglip_mlp_benchmark_shape():
-    """The siglip-mlp-benchmark graph shape (B=4, T=729, D=1152,
+    """The siglip-mlp-benchmark graph shape (crates/ipu-tests/src/main.rs:1627: B=4, T=729, D=1152,
     H=4304; two blocks, so the reference builds it as a Repeat over value
     sequences of [1, D, H] / [1, H, D] weights), seeded N(0, 1) inputs and
     N(0, 1/D) / N(0, 1/H) weights, against the evaluator: the hardware test's
