@@ -331,10 +331,18 @@ def run_ours(args):
         barrier(world)
         gather = gather_outputs(torch, world, y, o)
         tp = transformer_block_tp(torch, rank, world)
+        tp_peer = ar = None
+        if world <= 8:
+            ar = all_reduce_compare(ipuc, torch, rank, world)
+            tp_peer = transformer_block_tp(torch, rank, world, all_reduce="peer")
         if rank == 0:
             comps["gather_outputs"] = gather
             comps["transformer_block_tp"] = tp
             parity["config5_tp"] = tp.pop("parity")
+            if tp_peer is not None:
+                comps["all_reduce_64MiB"] = ar
+                comps["transformer_block_tp_peer"] = tp_peer
+                parity["config5_tp_peer"] = tp_peer.pop("parity")
         parity["pass"] = all_ranks_true(parity_pass(parity), world)
 
     # ---- CPU baseline (oracle, bounded sample, rank 0 at N=1) ----
@@ -761,15 +769,16 @@ def gather_outputs(torch, world, y, o):
             "bus_GB/s": round((world - 1) / world * total / (ms * 1e-3) / 1e9, 1), "collective": "NCCL all_gather"}
 
 
-def transformer_block_tp(torch, rank, world):
+def transformer_block_tp(torch, rank, world, all_reduce="nccl"):
     """Config 5 over all ranks through the sharded graph session (ipuc.tp):
     the session derives the Megatron split from the block's graph (QKV and
     MLP-up by columns, output and MLP-down projections by rows, one NCCL
-    all-reduce after each half).  Device time, max over ranks; TFLOP/s of the
+    all-reduce after each half; NCCL's, or with all_reduce="peer" the
+    library's peer-memory kernel).  Device time, max over ranks; TFLOP/s of the
     whole block."""
     from ipuc.tp import TensorParallelBlock
     B, S, d, H, ff = 4, 2048, 4096, 32, 16384
-    blk = TensorParallelBlock(B, S, d, H, ff, rank, world)
+    blk = TensorParallelBlock(B, S, d, H, ff, rank, world, all_reduce=all_reduce)
     g = torch.Generator(device="cuda")
     g.manual_seed(77)  # the same full weights and input on every rank
     full = {n: (torch.randn(shp, generator=g, device="cuda") * 0.02).half()
@@ -817,7 +826,56 @@ def transformer_block_tp(torch, rank, world):
     barrier(world)
     return {"parity": par, "ms": round(ms, 4), "tflops": round(blk.flop / (ms * 1e-3) / 1e12, 1), "flop": blk.flop,
             "parallelism": f"tp{world}", "steps": blk.session.plan.count("\n") - 1,
-            "collective": "2 NCCL all-reduces of 64 MiB (f16) per block, derived from the graph by the sharded session"}
+            "collective": ("2 NCCL all-reduces" if all_reduce == "nccl" else
+                           "2 peer-memory all-reduces (ipuc_peer_all_reduce_f16)") +
+                          " of 64 MiB (f16) per block, derived from the graph by the sharded session"}
+
+
+def all_reduce_compare(ipuc, torch, rank, world):
+    """The block's all-reduce alone (64 MiB of f16, [8192, 4096]): NCCL's
+    all_reduce against the library's peer-memory kernel on the same data.
+    Device time per call, max over ranks; algorithmic bandwidth = bytes / time.
+    Rank 0 checks the kernel's sum against NCCL's (bitwise at world 2, where
+    both round the exact sum once; within one f16 ulp of the f32 sum above)."""
+    import torch.distributed as dist
+    g = torch.Generator(device="cuda")
+    g.manual_seed(100 + rank)
+    x = torch.randn((8192, 4096), generator=g, device="cuda").half()
+    ref = x.clone()
+    y = torch.empty_like(x)
+    peer = ipuc.PeerAllReduce([x], [y])
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(10):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / 10, world)
+
+    t_peer = timed(lambda: peer.reduce(0, stream.cuda_stream))
+    ipuc.device_status(stream.cuda_stream)
+    work = ref.clone()
+    t_nccl = timed(lambda: dist.all_reduce(work.copy_(ref)))
+    dist.all_reduce(ref)
+    torch.cuda.synchronize()
+    diff = (y.float() - ref.float()).abs()
+    ulp = ref.float().abs().clamp(min=2.0 ** -14) * 2.0 ** -10
+    same = bool(torch.equal(y, ref))
+    within = bool((diff <= ulp).all())
+    peer.close()
+    nbytes = x.numel() * 2
+    return {"bytes": nbytes, "peer_ms": round(t_peer, 4), "nccl_ms_incl_copy": round(t_nccl, 4),
+            "peer_algbw_GB/s": round(nbytes / (t_peer * 1e-3) / 1e9, 1),
+            "nccl_algbw_GB/s": round(nbytes / (t_nccl * 1e-3) / 1e9, 1),
+            "bitwise_equal_nccl": same, "within_1ulp_of_nccl": within,
+            "note": "the NCCL leg includes a 64 MiB device copy that restores its in-place input"}
 
 
 # ---------------------------------------------------------------------------

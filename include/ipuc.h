@@ -412,6 +412,36 @@ ipuc_status ipuc_launch(const ipuc_kernel_spec *spec, const ipuc_tensor *output,
                         int32_t input_count, const uint32_t *scalars, int32_t scalar_count, void *workspace,
                         uint64_t workspace_bytes, ipuc_stream stream);
 
+/* ---- Peer-memory all-reduce (multi-GPU sum after a row-split GEMM) ----
+ * The sharded session's all-reduce (transformer block out-proj / MLP-down,
+ * Megatron split) done by this library's kernel over NVLink peer memory in
+ * place of ncclAllReduce.  Its arithmetic is the reference's partial-sum
+ * kernel ipu_stack_reduce_sum_f16 (device/reduce_add_f16.S:31-72, ABI
+ * crates/ipu-codegen/src/kernel.rs:1264-1274) with the partials held by
+ * other GPUs: out = sum over ranks in rank order, in f32, rounded once to f16,
+ * identical bits on every rank.
+ *
+ * Buffers are shared between the ranks' processes through CUDA IPC:
+ * ipuc_ipc_handle exports any device pointer of this process (64-byte handle
+ * plus the pointer's offset inside its allocation), ipuc_ipc_open maps a
+ * peer's handle into this process, ipuc_ipc_close unmaps it.  Each rank owns
+ * one signal area of ipuc_peer_signal_bytes() bytes, zero-filled before any
+ * rank's first call (and re-created after a timed-out call). */
+uint64_t ipuc_peer_signal_bytes(void);
+ipuc_status ipuc_ipc_handle(const void *device_ptr, void *handle_out, uint64_t size, uint64_t *offset);
+ipuc_status ipuc_ipc_open(const void *handle, uint64_t offset, void **device_ptr);
+ipuc_status ipuc_ipc_close(void *device_ptr);
+/* inputs[q], outputs[q], signals[q]: this process's mapping of rank q's input,
+ * output and signal area (its own at q == rank).  Every rank calls with the
+ * same world and element_count (a multiple of 8 * world, 2 <= world <= 8);
+ * buffers 16-byte aligned; input and output may be the same buffer.  All
+ * ranks' launches must be able to run at the same time (one launch per GPU,
+ * never two ranks on one GPU).  Waits on peers are bounded (2 s): on expiry
+ * the kernel sets the device error word (ipuc_device_status ->
+ * IPUC_ERR_DEVICE_TIMEOUT) and returns. */
+ipuc_status ipuc_peer_all_reduce_f16(void *const *inputs, void *const *outputs, void *const *signals, int32_t rank,
+                                     int32_t world, uint64_t element_count, ipuc_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

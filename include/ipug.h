@@ -126,6 +126,15 @@ ipuc_status ipug_session_read(ipug_session *s, int32_t value, void *host, uint64
 /* Device pointer of a value's buffer (for callers that keep data on the GPU). */
 void *ipug_session_device_ptr(ipug_session *s, int32_t value);
 ipuc_status ipug_session_run(ipug_session *s, ipuc_stream stream);
+/* Collective over the session's ranks (every rank calls it, after open and
+ * before the next run): run the session's all-reduce steps with this
+ * library's peer-memory kernel (ipuc_peer_all_reduce_f16) instead of
+ * ncclAllReduce.  The ranks exchange CUDA IPC handles of the all-reduce
+ * buffers and of a signal area over the session's NCCL communicator.  An
+ * all-reduce whose element count is not a multiple of 8 * world, or a world
+ * above 8, stays on NCCL.  `enable` 0 goes back to NCCL (the mappings stay
+ * until close).  A world-1 session has no all-reduce: a no-op. */
+ipuc_status ipug_session_peer_reduce(ipug_session *s, int32_t enable, ipuc_stream stream);
 
 /* ---- Per-op diagnostic (build_diagnostic_package, crates/ipu-codegen/src/
  * package.rs:543; service_checkpoint, crates/ipu-tests/src/diagnostic.rs:

@@ -38,6 +38,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <sstream>
@@ -49,6 +50,7 @@
 namespace ipuc {
 void set_error(const std::string &msg);
 ipuc_status fail(ipuc_status st, const std::string &msg);
+ipuc_status cuda_fail(cudaError_t err, const char *what);
 }  // namespace ipuc
 
 namespace {
@@ -959,6 +961,13 @@ struct ipug_session {
   std::vector<void *> buffers;  // by local value; nullptr = fused away
   std::vector<void *> extra;    // by local value: all-gather staging
   ncclComm_t comm = nullptr;
+  // Peer-memory all-reduce (ipug_session_peer_reduce): this process's mapping
+  // of every rank's buffer, by local value, and of every rank's signal area.
+  bool peer = false;
+  void *signal = nullptr;
+  std::vector<void *> peer_signal;
+  std::map<int32_t, std::vector<void *>> peer_buffers;
+  std::vector<void *> peer_opened;  // mappings of other ranks' memory, closed at exit
   ~ipug_session() {
     bool any = comm != nullptr;
     for (void *p : buffers) any = any || p != nullptr;
@@ -968,6 +977,8 @@ struct ipug_session {
       if (p) cudaFree(p);
     for (void *p : extra)
       if (p) cudaFree(p);
+    for (void *p : peer_opened) ipuc_ipc_close(p);
+    if (signal) cudaFree(signal);
     if (comm) nccl().comm_destroy(comm);
   }
 };
@@ -1039,6 +1050,12 @@ ipuc_status run_step(ipug_session &s, const Step &st, cudaStream_t stream) {
       return IPUC_OK;
     }
     case StepKind::AllReduce: {
+      if (s.peer) {
+        const auto in = s.peer_buffers.find(st.in0), out = s.peer_buffers.find(st.out);
+        if (in != s.peer_buffers.end() && out != s.peer_buffers.end())
+          return ipuc_peer_all_reduce_f16(in->second.data(), out->second.data(), s.peer_signal.data(), s.rank,
+                                          s.world, st.count, stream);
+      }
       const ncclResult_t r = nccl().all_reduce(P(st.in0), P(st.out), st.count, ncclFloat16, ncclSum, s.comm, stream);
       return r == ncclSuccess ? IPUC_OK : nccl_fail(r, "session all-reduce");
     }
@@ -1508,6 +1525,84 @@ ipuc_status ipug_session_run(ipug_session *s, ipuc_stream stream) {
     const ipuc_status rc = run_step(*s, st, stream);
     if (rc != IPUC_OK) return rc;
   }
+  return IPUC_OK;
+}
+
+namespace {
+// One exchanged entry: a CUDA IPC handle and the pointer's offset inside its allocation.
+constexpr uint64_t kIpcEntry = 72;
+
+ipuc_status exchange_peer_maps(ipug_session &s, cudaStream_t stream) {
+  std::vector<int32_t> values;
+  for (const Step &st : s.lowered.steps) {
+    if (st.kind != StepKind::AllReduce || st.count % (8ull * (uint64_t)s.world) != 0) continue;
+    for (int32_t v : {st.in0, st.out})
+      if (std::find(values.begin(), values.end(), v) == values.end()) values.push_back(v);
+  }
+  const uint64_t sig_bytes = ipuc_peer_signal_bytes();
+  cudaError_t me = cudaMalloc(&s.signal, sig_bytes);
+  if (me == cudaSuccess) me = cudaMemsetAsync(s.signal, 0, sig_bytes, stream);
+  if (me != cudaSuccess) return ipuc::cuda_fail(me, "session peer-reduce signal area");
+  const uint64_t entries = values.size() + 1, blob = entries * kIpcEntry;
+  std::vector<uint8_t> mine(blob), all(blob * (uint64_t)s.world);
+  for (uint64_t e = 0; e < entries; ++e) {
+    void *p = e == 0 ? s.signal : s.buffers[values[e - 1]];
+    uint64_t offset = 0;
+    if (ipuc_status st = ipuc_ipc_handle(p, mine.data() + e * kIpcEntry, 64, &offset)) return st;
+    std::memcpy(mine.data() + e * kIpcEntry + 64, &offset, 8);
+  }
+  void *send = nullptr, *recv = nullptr;
+  cudaError_t ce = cudaMalloc(&send, blob);
+  if (ce == cudaSuccess) ce = cudaMalloc(&recv, blob * (uint64_t)s.world);
+  ncclResult_t nr = ncclSuccess;
+  if (ce == cudaSuccess) ce = cudaMemcpyAsync(send, mine.data(), blob, cudaMemcpyHostToDevice, stream);
+  // The gather also orders every rank's signal-area memset before any peer's first flag.
+  if (ce == cudaSuccess) nr = nccl().all_gather(send, recv, blob, ncclUint8, s.comm, stream);
+  if (ce == cudaSuccess && nr == ncclSuccess)
+    ce = cudaMemcpyAsync(all.data(), recv, all.size(), cudaMemcpyDeviceToHost, stream);
+  if (ce == cudaSuccess && nr == ncclSuccess) ce = cudaStreamSynchronize(stream);
+  if (send) cudaFree(send);
+  if (recv) cudaFree(recv);
+  if (nr != ncclSuccess) return nccl_fail(nr, "session peer-reduce handle exchange");
+  if (ce != cudaSuccess) return ipuc::cuda_fail(ce, "session peer-reduce handle exchange");
+  s.peer_signal.assign(s.world, nullptr);
+  for (int32_t v : values) s.peer_buffers[v].assign(s.world, nullptr);
+  for (int32_t q = 0; q < s.world; ++q) {
+    for (uint64_t e = 0; e < entries; ++e) {
+      void *local = e == 0 ? s.signal : s.buffers[values[e - 1]];
+      void *mapped = local;
+      if (q != s.rank) {
+        const uint8_t *entry = all.data() + (uint64_t)q * blob + e * kIpcEntry;
+        uint64_t offset = 0;
+        std::memcpy(&offset, entry + 64, 8);
+        if (ipuc_status st = ipuc_ipc_open(entry, offset, &mapped)) return st;
+        s.peer_opened.push_back(mapped);
+      }
+      if (e == 0) s.peer_signal[q] = mapped;
+      else s.peer_buffers[values[e - 1]][q] = mapped;
+    }
+  }
+  return IPUC_OK;
+}
+}  // namespace
+
+ipuc_status ipug_session_peer_reduce(ipug_session *s, int32_t enable, ipuc_stream stream) {
+  if (!s) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session_peer_reduce: null session");
+  if (s->world == 1 || s->world > 8 || s->buffers.empty()) {
+    s->peer = false;
+    return IPUC_OK;
+  }
+  if (!enable) {
+    s->peer = false;
+    return IPUC_OK;
+  }
+  if (!s->comm) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session_peer_reduce: no communicator");
+  DeviceGuard guard(s->device);
+  if (!s->signal) {
+    const ipuc_status st = exchange_peer_maps(*s, stream);
+    if (st != IPUC_OK) return st;
+  }
+  s->peer = true;
   return IPUC_OK;
 }
 

@@ -63,6 +63,11 @@ SIGNATURES = {
     "ipuc_merge_heads_f16": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ipuc_query_abi": (_i32, [_vp, _i32, _vp]),
     "ipuc_launch": (_i32, [_vp, _vp, _vp, _i32, _vp, _i32, _vp, _u64, _vp]),
+    "ipuc_peer_signal_bytes": (_u64, []),
+    "ipuc_ipc_handle": (_i32, [_vp, _vp, _u64, ctypes.POINTER(_u64)]),
+    "ipuc_ipc_open": (_i32, [_vp, _u64, ctypes.POINTER(_vp)]),
+    "ipuc_ipc_close": (_i32, [_vp]),
+    "ipuc_peer_all_reduce_f16": (_i32, [_vp, _vp, _vp, _i32, _i32, _u64, _vp]),
 }
 
 
@@ -426,3 +431,59 @@ def launch(spec, out, inputs=(), scalars=(), workspace=None, stream=None):
     ws = workspace.numel() * workspace.element_size() if workspace is not None else 0
     call("ipuc_launch", ctypes.byref(spec), ctypes.byref(o), arr, len(ins), sc, len(scalars), _ptr(workspace), ws,
          _stream(stream))
+
+
+# ---- peer-memory all-reduce over NVLink (one process per GPU) -------------
+
+class PeerAllReduce:
+    """Sum of f16 tensors across the ranks of a torch.distributed group with
+    this library's peer-memory kernel (ipuc_peer_all_reduce_f16).  `inputs`
+    and `outputs` are lists of this rank's device tensors, the same shapes on
+    every rank; the constructor is collective (CUDA IPC handles travel through
+    torch.distributed.all_gather_object).  reduce(i) sums inputs[i] of all
+    ranks into outputs[i] of every rank, stream-ordered."""
+
+    def __init__(self, inputs, outputs, group=None):
+        import torch
+        import torch.distributed as dist
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.signal = torch.zeros(int(lib().ipuc_peer_signal_bytes()), dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        self._keep = list(inputs) + list(outputs)
+        mine = []
+        for t in [self.signal] + list(inputs) + list(outputs):
+            h = ctypes.create_string_buffer(64)
+            off = _u64(0)
+            call("ipuc_ipc_handle", _ptr(t), h, 64, ctypes.byref(off))
+            mine.append((h.raw, off.value))
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=group)
+        self._opened = []
+        table = []
+        for q in range(self.world):
+            row = []
+            for e, (h, off) in enumerate(every[q]):
+                if q == self.rank:
+                    row.append(_ptr(([self.signal] + list(inputs) + list(outputs))[e]))
+                    continue
+                p = _vp()
+                call("ipuc_ipc_open", h, off, ctypes.byref(p))
+                self._opened.append(p.value)
+                row.append(p.value)
+            table.append(row)
+        n = len(inputs)
+        arr = _vp * self.world
+        self._sig = arr(*[table[q][0] for q in range(self.world)])
+        self._in = [arr(*[table[q][1 + i] for q in range(self.world)]) for i in range(n)]
+        self._out = [arr(*[table[q][1 + n + i] for q in range(self.world)]) for i in range(n)]
+        self._count = [t.numel() for t in inputs]
+        dist.barrier(group=group)
+
+    def reduce(self, i: int = 0, stream=None):
+        call("ipuc_peer_all_reduce_f16", self._in[i], self._out[i], self._sig, self.rank, self.world,
+             self._count[i], _stream(stream))
+
+    def close(self):
+        for p in self._opened:
+            lib().ipuc_ipc_close(p)
+        self._opened = []

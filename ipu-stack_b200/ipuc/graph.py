@@ -43,6 +43,7 @@ _G_SIGS = {
     "ipug_session_read": (ctypes.c_int32, [_vp, ctypes.c_int32, _vp, ctypes.c_uint64, _vp]),
     "ipug_session_device_ptr": (_vp, [_vp, ctypes.c_int32]),
     "ipug_session_run": (ctypes.c_int32, [_vp, _vp]),
+    "ipug_session_peer_reduce": (ctypes.c_int32, [_vp, ctypes.c_int32, _vp]),
     "ipug_session_profile": (ctypes.c_int32, [_vp, _vp, ctypes.c_char_p, ctypes.c_uint64,
                                               ctypes.POINTER(ctypes.c_uint64)]),
     "ipug_session_profile_capnp": (ctypes.c_int32, [_vp, _vp, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint64,
@@ -379,6 +380,11 @@ class Session:
 
     def run(self, stream=None):
         self._call("ipug_session_run", self._s, _stream(stream))
+
+    def peer_reduce(self, enable: bool = True, stream=None):
+        """Collective: run the all-reduce steps with the library's peer-memory
+        kernel (True) or with NCCL (False)."""
+        self._call("ipug_session_peer_reduce", self._s, int(bool(enable)), _stream(stream))
 
     def profile(self, stream=None) -> dict:
         need = ctypes.c_uint64(0)

@@ -58,9 +58,12 @@ class TensorParallelBlock:
     """y = h + W2^T GELU(W1^T h), h = x + Wo^T attn(x Wq, x Wk, x Wv), one rank
     of a sharded graph session (this rank's weight slices resident on its GPU,
     f16, row-major [in, out]).  With world > 1, torch.distributed must be
-    initialised: rank 0's NCCL unique id reaches the others through it."""
+    initialised: rank 0's NCCL unique id reaches the others through it.
+    all_reduce "peer" runs the two all-reduces with the library's
+    peer-memory kernel over NVLink instead of ncclAllReduce."""
 
-    def __init__(self, batch: int, seq: int, d: int, heads: int, ff: int, rank: int, world: int, group=None):
+    def __init__(self, batch: int, seq: int, d: int, heads: int, ff: int, rank: int, world: int, group=None,
+                 all_reduce: str = "nccl"):
         import torch
         from .graph import Session, nccl_unique_id
         self.torch = torch
@@ -78,6 +81,10 @@ class TensorParallelBlock:
         self.session = Session(self.graph, device=torch.cuda.current_device(), rank=rank, world=world,
                                nccl_id=nccl_id)
         self.out = self.session.tensor(self.y, (batch * seq, d))
+        if world > 1 and all_reduce == "peer":
+            self.session.peer_reduce(True, torch.cuda.current_stream().cuda_stream)
+        elif all_reduce not in ("nccl", "peer"):
+            raise ValueError("all_reduce must be 'nccl' or 'peer'")
 
     def load(self, weights: dict) -> None:
         """Copy this rank's slices out of full f16 torch tensors wq, wk, wv, wo

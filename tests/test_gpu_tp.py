@@ -30,9 +30,9 @@ def block_inputs():
     return inputs[x].reshape(B * S, d), weights, ref
 
 
-def run_rank(rank, world, x, weights):
+def run_rank(rank, world, x, weights, all_reduce="nccl"):
     from ipuc.tp import TensorParallelBlock
-    blk = TensorParallelBlock(B, S, d, H, ff, rank, world)
+    blk = TensorParallelBlock(B, S, d, H, ff, rank, world, all_reduce=all_reduce)
     blk.load({n: torch.from_numpy(a).half() for n, a in weights.items()})
     y = blk.forward(torch.from_numpy(x).half().cuda())
     torch.cuda.synchronize()
@@ -46,21 +46,22 @@ def test_tp_block_one_rank_matches_graph_oracle():
     assert ok, msg
 
 
-def _nccl_worker(rank, world, port, q):
+def _nccl_worker(rank, world, port, q, all_reduce="nccl"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
         x, weights, ref = block_inputs()
-        got = run_rank(rank, world, x, weights)
+        got = run_rank(rank, world, x, weights, all_reduce)
         q.put((rank,) + f16_close(got, ref))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp_block_two_ranks_nccl():
+@pytest.mark.parametrize("all_reduce", ["nccl", "peer"])
+def test_tp_block_two_ranks_nccl(all_reduce):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -68,7 +69,7 @@ def test_tp_block_two_ranks_nccl():
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q, all_reduce)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in procs)
