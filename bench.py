@@ -826,8 +826,8 @@ def transformer_block_tp(torch, rank, world, all_reduce="nccl"):
     barrier(world)
     return {"parity": par, "ms": round(ms, 4), "tflops": round(blk.flop / (ms * 1e-3) / 1e12, 1), "flop": blk.flop,
             "parallelism": f"tp{world}", "steps": blk.session.plan.count("\n") - 1,
-            "collective": ("2 NCCL all-reduces" if all_reduce == "nccl" else
-                           "2 peer-memory all-reduces (ipuc_peer_all_reduce_f16)") +
+            "collective": {"nccl": "2 NCCL all-reduces",
+                           "peer": "2 peer-memory all-reduces (ipuc_peer_all_reduce_f16)"}[all_reduce] +
                           " of 64 MiB (f16) per block, derived from the graph by the sharded session"}
 
 

@@ -62,10 +62,12 @@ __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" 
 __device__ bool peer_barrier(const PeerPtrs &a, int rank, int world, int phase, uint32_t epoch, uint32_t *err) {
   __shared__ int s_ok;
   const int b = blockIdx.x;
+  // Every thread's own stores into peers' memory (and local ones peers will
+  // read) complete at system scope before the CTA's signal can be seen.
+  fence_sys();
   __syncthreads();
   if (threadIdx.x == 0) {
     s_ok = 1;
-    fence_sys();
     for (int q = 0; q < world; ++q)
       st_release_sys(a.sig[q] + ((uint64_t)phase * kMaxWorld + rank) * kBlocks + b, epoch);
   }
@@ -118,7 +120,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint64_t base = (uint64_t)rank * slice_vecs;
   const uint64_t lo = base + (uint64_t)b * chunk;
   const uint64_t hi = base + min(slice_vecs, (uint64_t)(b + 1) * chunk);
-  constexpr int U = 2;  // vectors per thread per pass: W * U 16-byte peer loads in flight
+  // vectors per thread per pass: W * U = 16 loads of 16 bytes in flight per thread
+  constexpr int U = W <= 2 ? 8 : W <= 4 ? 4 : 2;
   for (uint64_t i0 = lo + threadIdx.x; i0 < hi; i0 += (uint64_t)kThreads * U) {
     uint4 v[U][W];
 #pragma unroll
@@ -240,3 +243,4 @@ extern "C" ipuc_status ipuc_peer_all_reduce_f16(void *const *inputs, void *const
   }
   return check_launch("peer_all_reduce_kernel");
 }
+

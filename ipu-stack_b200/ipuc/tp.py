@@ -81,10 +81,10 @@ class TensorParallelBlock:
         self.session = Session(self.graph, device=torch.cuda.current_device(), rank=rank, world=world,
                                nccl_id=nccl_id)
         self.out = self.session.tensor(self.y, (batch * seq, d))
+        if all_reduce not in ("nccl", "peer"):
+            raise ValueError("all_reduce must be 'nccl' or 'peer'")
         if world > 1 and all_reduce == "peer":
             self.session.peer_reduce(True, torch.cuda.current_stream().cuda_stream)
-        elif all_reduce not in ("nccl", "peer"):
-            raise ValueError("all_reduce must be 'nccl' or 'peer'")
 
     def load(self, weights: dict) -> None:
         """Copy this rank's slices out of full f16 torch tensors wq, wk, wv, wo

@@ -1,7 +1,8 @@
 """Peer-memory all-reduce (ipuc_peer_all_reduce_f16) on two GPUs, one process
 each: the kernel's f16 sum against the exactly rounded sum of the two ranks'
 values and against NCCL's all_reduce, over several calls in a row (the
-per-call counters of the signal area), in place and out of place, and the
+per-call counters of the signal area), in place and out of place, back to
+back on the stream with the data changing between calls, and the
 device error word clear afterwards.  The stand-in for ncclAllReduce in the
 sharded session's row-split GEMMs; its sum is the reference's partial sum
 (device/reduce_add_f16.S:31-72) over GPUs instead of tiles."""
@@ -60,6 +61,28 @@ def _worker(rank, world, port, q):
                     msgs.append(f"call {call} size {n}: differs from NCCL")
                 if i == 1 and not torch.equal(inplace, ys[1]):
                     msgs.append(f"call {call}: in-place result differs")
+        # back to back on the stream with no host synchronisation, the data
+        # changing between calls: a missing ordering between one call's stores
+        # and the next call's reads shows up as the previous call's values
+        seq = []
+        for call in range(8):
+            i = call % 2
+            g = torch.Generator(device="cuda")
+            g.manual_seed(7000 + 10 * call + rank)
+            xs[i].copy_(torch.randn(sizes[i], generator=g, device="cuda").half())
+            ar.reduce(i, stream)
+            seq.append(ys[i].clone())
+        torch.cuda.synchronize()
+        for call in range(8):
+            i = call % 2
+            parts = []
+            for r in range(world):
+                g = torch.Generator(device="cuda")
+                g.manual_seed(7000 + 10 * call + r)
+                parts.append(torch.randn(sizes[i], generator=g, device="cuda").half())
+            exact = torch.stack([p.double() for p in parts]).sum(0).half()
+            if not torch.equal(seq[call], exact):
+                msgs.append(f"back-to-back call {call}: {int((seq[call] != exact).sum())} elements differ")
         ipuc.device_status(stream)
         ar.close()
         q.put((rank, not msgs, "; ".join(msgs)))
