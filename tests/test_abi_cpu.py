@@ -99,3 +99,44 @@ def test_ipuc_error_carries_status():
     with pytest.raises(ipuc.IpucError) as e:
         ipuc.call("ipuc_gelu_f16", None, None, 5, None)
     assert e.value.status == ipuc.ERR_INVALID_ARGUMENT
+
+
+def test_peer_all_reduce_argument_checks():
+    """ipuc_peer_all_reduce_f16 rejects bad pointer tables, worlds, ranks,
+    element counts and alignment before touching the device."""
+    L = ipuc.lib()
+    arr = ctypes.c_void_p * 2
+    good = arr(0x1000, 0x2000)
+    sig = arr(0x3000, 0x4000)
+    assert L.ipuc_peer_signal_bytes() > 0 and L.ipuc_peer_signal_bytes() % 16 == 0
+    cases = [
+        ((None, good, sig, 0, 2, 1024), 1, "null pointer table"),
+        ((good, good, sig, 0, 1, 1024), 1, "world"),
+        ((good, good, sig, 0, 9, 1024), 1, "world"),
+        ((good, good, sig, 2, 2, 1024), 1, "rank"),
+        ((good, good, sig, 0, 2, 1000), 1, "multiple of 8 * world"),
+        ((good, arr(0x2000, None), sig, 0, 2, 1024), 1, "null buffer"),
+        ((arr(0x1001, 0x2000), good, sig, 0, 2, 1024), 3, "16-byte aligned"),
+    ]
+    for args, code, text in cases:
+        st = L.ipuc_peer_all_reduce_f16(*args, None)
+        assert st == code, (args, st)
+        assert text in L.ipuc_last_error_string().decode()
+    assert L.ipuc_peer_all_reduce_f16(good, good, sig, 0, 2, 0, None) == 0  # nothing to do
+
+
+def test_ipc_argument_checks():
+    L = ipuc.lib()
+    off = ctypes.c_uint64(0)
+    buf = ctypes.create_string_buffer(64)
+    assert L.ipuc_ipc_handle(None, buf, 64, ctypes.byref(off)) == 1
+    assert L.ipuc_ipc_handle(ctypes.c_void_p(0x1000), buf, 32, ctypes.byref(off)) == 1
+    p = ctypes.c_void_p()
+    assert L.ipuc_ipc_open(None, 0, ctypes.byref(p)) == 1
+    assert L.ipuc_ipc_close(None) == 1
+
+
+def test_session_peer_reduce_rejects_null_session():
+    from ipuc.graph import glib
+    assert glib().ipug_session_peer_reduce(None, 1, None) == 1
+    assert "null session" in ipuc.lib().ipuc_last_error_string().decode()
