@@ -113,3 +113,23 @@ def test_graph_shard_matches_closed_form_plan():
             assert (sl[w["wo"]]["slice"], tuple(sl[w["wo"]]["range"])) == ("rows", sh.qkv_cols)
             assert (sl[w["w1"]]["slice"], tuple(sl[w["w1"]]["range"])) == ("columns", sh.ff_cols)
             assert (sl[w["w2"]]["slice"], tuple(sl[w["w2"]]["range"])) == ("rows", sh.ff_cols)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_all_reduce_steps_line_up_across_ranks(world):
+    """The peer-memory all-reduce pairs every rank's buffers by the position of
+    the all-reduce steps in each rank's plan (local value ids differ between
+    ranks), so every rank's plan must hold the same all-reduces, in the same
+    order, over the same shapes, with element counts the kernel accepts."""
+    import re
+    from ipuc.tp import block_graph
+    g, _, _, _ = block_graph(4, 2048, 4096, 32, 16384)
+    seqs = []
+    for rank in range(world):
+        steps = [ln for ln in g.plan(rank=rank, world=world).splitlines() if "all_reduce" in ln]
+        seqs.append([re.sub(r"out=[lv]\d+", "out=", ln) for ln in steps])
+    assert len(seqs[0]) == 2
+    assert all(s == seqs[0] for s in seqs)
+    for ln in seqs[0]:
+        dims = [int(d) for d in re.search(r"\[([\d,]+)\]", ln).group(1).split(",")]
+        assert int(np.prod(dims)) % (8 * world) == 0
