@@ -331,14 +331,21 @@ def run_ours(args):
         barrier(world)
         gather = gather_outputs(torch, world, y, o)
         tp = transformer_block_tp(torch, rank, world)
-        tp_peer = ar = None
+        tp_peer = ar = peer_error = None
         if world <= 8:
-            ar = all_reduce_compare(ipuc, torch, rank, world)
-            tp_peer = transformer_block_tp(torch, rank, world, all_reduce="peer")
+            # supplementary: a failure here (e.g. CUDA IPC refused) is reported, not fatal
+            try:
+                ar = all_reduce_compare(ipuc, torch, rank, world)
+                tp_peer = transformer_block_tp(torch, rank, world, all_reduce="peer")
+            except Exception as e:  # noqa: BLE001
+                peer_error = repr(e)[:300]
+                tp_peer = None
         if rank == 0:
             comps["gather_outputs"] = gather
             comps["transformer_block_tp"] = tp
             parity["config5_tp"] = tp.pop("parity")
+            if peer_error is not None:
+                comps["peer_all_reduce_error"] = peer_error
             if tp_peer is not None:
                 comps["all_reduce_64MiB"] = ar
                 comps["transformer_block_tp_peer"] = tp_peer
