@@ -963,7 +963,7 @@ struct ipug_session {
   ncclComm_t comm = nullptr;
   // Peer-memory all-reduce (ipug_session_peer_reduce): this process's mapping
   // of every rank's buffer, by local value, and of every rank's signal area.
-  bool peer = false;
+  bool peer = false, peer_mapped = false;
   void *signal = nullptr;
   std::vector<void *> peer_signal;
   std::map<int32_t, std::vector<void *>> peer_buffers;
@@ -1598,9 +1598,13 @@ ipuc_status ipug_session_peer_reduce(ipug_session *s, int32_t enable, ipuc_strea
   }
   if (!s->comm) return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT, "session_peer_reduce: no communicator");
   DeviceGuard guard(s->device);
-  if (!s->signal) {
+  if (!s->peer_mapped) {
+    if (s->signal)
+      return ipuc::fail(IPUC_ERR_INVALID_ARGUMENT,
+                        "session_peer_reduce: an earlier handle exchange failed; re-open the session");
     const ipuc_status st = exchange_peer_maps(*s, stream);
     if (st != IPUC_OK) return st;
+    s->peer_mapped = true;
   }
   s->peer = true;
   return IPUC_OK;
